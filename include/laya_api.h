@@ -1,0 +1,116 @@
+/* C ABI of the Laya B200 engine (liblaya_b200.so).
+ *
+ * The first ten declarations are the reference engine's ABI, unchanged in name, signature and
+ * meaning (mauimauer/layamd src/laya_api.h:5-19, implemented at src/engine.hip:543-559), so the
+ * reference's ctypes server (server/laya_server.py:18-31), its parity tool (src/test_parity.cpp)
+ * and its bench tool (src/bench_engine.cpp) bind to this library without change. Everything after
+ * them is an addition with no counterpart in the reference.
+ *
+ * Threading: a handle is driven by one caller thread at a time, as in the reference
+ * (docs/architecture.md:84-85). Calls are synchronous: forward returns after the results are in
+ * the caller's arrays.
+ */
+#pragma once
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Loads `dir` (model.safetensors, encoder/config.json, rl_agent_config.json) onto the GPUs named by
+ * LAYA_DEVICES (default: the current device) and sizes every buffer for LAYA_MAX_TOKENS rows.
+ * Replaces src/laya_api.h:5. The reference exits the process on a load error; this library prints
+ * the reason and returns NULL instead. */
+void* laya_create(const char* dir);
+
+/* B questions in one call. ids/markers are concatenated per question; markers are positions within
+ * that question's sequence. logits receive sum(nmark) raw scorer logits in input order, act B*n_act
+ * raw act-head logits. Returns 0, or -1 without touching the outputs when any 1<=lens[b]<=max_len,
+ * 1<=nmark[b]<=255 or 0<=marker<lens[b] fails. Replaces src/laya_api.h:8-9
+ * (src/engine.hip:489-539). Also returns -2 when the GPU reported an error for this call. */
+int laya_forward_batch(void* h, int B, const int* lens, const int* ids, const int* nmark, const int* markers,
+                       const int* qtypes, float* logits, float* act);
+
+/* Single-question form; S is ignored and valid_len is the length. Input errors are ignored
+ * silently, as in the reference. Replaces src/laya_api.h:10-11 (src/engine.hip:549-551). */
+void laya_forward(void* h, const int* ids, int S, int valid_len, const int* markers, int K, int qtype,
+                  float* logits, float* act);
+
+int laya_n_act(void* h);       /* len(act_costs)+1 from rl_agent_config.json (src/laya_api.h:12) */
+int laya_max_len(void* h);     /* max_len from rl_agent_config.json (src/laya_api.h:13) */
+int laya_max_markers(void* h); /* 255 (src/laya_api.h:14) */
+/* Calibration temperature of a question type (src/laya_api.h:15); 1.0 for a qtype outside the
+ * configured list (the reference does not check the index). */
+float laya_temperature(void* h, int qtype);
+/* Per-stage device-time table printed to stdout, divided by `iters` (src/laya_api.h:16). Stages are
+ * timed only while profiling is on (LAYA_PROFILE set at load, or laya_prof_enable). */
+void laya_prof_report(void* h, int iters);
+void laya_prof_reset(void* h); /* src/laya_api.h:17 */
+/* Chooses the GEMM tile width for every (M bucket, N, K) the model can hit up front, so serving
+ * never tunes on the request path (src/laya_api.h:19). */
+void laya_tune_all(void* h);
+
+/* ----------------------------------------------------------------- additions (no reference
+ * counterpart) */
+
+/* Releases every device and host resource of the handle. */
+void laya_destroy(void* h);
+
+/* laya_create with an explicit precision and device list.
+ * precision 0: bf16 operands, fp32 accumulation and fp32 residual stream (production path).
+ * precision 1: fp32-parity mode: every GEMM runs as three bf16 products on hi/lo splits of both
+ *              operands (A_hi*W_hi + A_hi*W_lo + A_lo*W_hi) and attention runs in fp32.
+ * devices: comma-separated CUDA device ordinals ("0", "0,1,2,3"); NULL or "" uses LAYA_DEVICES or
+ * the current device. With several devices, each forward call shards its questions across them. */
+void* laya_create_ex(const char* dir, int precision, const char* devices);
+
+/* Number of devices (replicas) the handle runs on. */
+int laya_num_devices(void* h);
+
+/* Turns per-stage profiling on or off (CUDA events around every launch; graphs are bypassed while
+ * it is on). */
+void laya_prof_enable(void* h, int on);
+
+/* Copies the accumulated time (ms) and launch count of stage `name` (e.g. "gemm_qkv"); returns 0 or
+ * -1 if the stage was never timed. */
+int laya_prof_get(void* h, const char* name, double* ms, long long* launches);
+
+/* Packs a batch exactly like laya_forward_batch would (validation included) and reports the pass
+ * layout without touching a GPU: n_passes, and for each pass its first question, question count and
+ * packed row count (arrays of capacity `cap`). Returns the number of passes or -1 on invalid input. */
+int laya_plan_passes(void* h, int B, const int* lens, const int* nmark, const int* markers, int cap,
+                     int* pass_first, int* pass_count, int* pass_rows);
+
+/* Same packing rules as laya_plan_passes for a configuration given by value, with no handle
+ * (max_len, pass_tokens, max_seqs); for host-side tests. */
+int laya_plan_passes_cfg(int max_len, int pass_tokens, int max_seqs, int B, const int* lens, const int* nmark,
+                         const int* markers, int cap, int* pass_first, int* pass_count, int* pass_rows);
+
+/* Benchmark support: validates, packs and uploads one batch (it must fit one pass per device) and
+ * keeps it resident; laya_replay then runs the staged pass `iters` times back to back on every
+ * device with the inputs already in HBM and writes the device time of the slowest device, measured
+ * with CUDA events on the engine's stream, to *ms. laya_staged_results copies the last replay's
+ * outputs out like laya_forward_batch. Return 0 or a negative error. */
+int laya_stage(void* h, int B, const int* lens, const int* ids, const int* nmark, const int* markers,
+               const int* qtypes);
+int laya_replay(void* h, int iters, double* ms);
+int laya_staged_results(void* h, float* logits, float* act);
+
+/* Writes the residual stream after the embedding, after every encoder layer (before the final
+ * norm), after the final norm + type embedding, and after each head layer for the last forward call
+ * when dumping is on: files emb.bin, enc<i>.bin, final.bin, head<i>.bin (fp32, one row per packed
+ * token of pass 0, sequences back to back in input order; head<last>.bin holds the gathered rows:
+ * markers of every question in order, then one CLS row per question). NULL turns dumping off. */
+int laya_set_dump_dir(void* h, const char* dir);
+
+/* Isolated encoder GEMM on caller-owned device memory (the GEMM sweep and kernel tests):
+ * out = epilogue(A[planes][M][K] * W[planes][N][K]^T). epi: 0 store, 1 store with RoPE on columns
+ * < rope_cols, 2 GeGLU (W interleaved in groups of bn/2, out has geglu_I columns), 3 fp32 residual
+ * add into resid[M][N]. out_mode: 0 bf16, 1 bf16 hi/lo planes, 2 fp32. act: 0 none, 1 ReLU, 2 GELU.
+ * bn: 128 or 256. planes 2 selects the three-product fp32 emulation. stream may be NULL. With
+ * sync != 0 the call waits for the GPU and returns -100-code if the kernel reported an error. */
+int laya_b200_gemm(const void* A, const void* W, void* out, float* resid, const float* bias, int M, int N, int K,
+                   int planes, int epi, int out_mode, int act, int bn, const float* cos_t, const float* sin_t,
+                   const int* pos, int rope_cols, int geglu_I, void* stream, int sync);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,125 @@
+// Host-side launchers for the sm_100a kernels of the Laya B200 engine. Device pointers only; every
+// launcher enqueues on the given stream and never synchronises, so a whole pass can be captured in
+// one CUDA graph.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace laya {
+
+typedef __nv_bfloat16 bf16;
+
+// ------------------------------------------------------------------ GEMM (tcgen05 + TMA + TMEM)
+// C[M, N] = A[M, K] * B[N, K]^T with both operands K-major bf16 ("nn.Linear" layout: B is the
+// weight as stored, [out, in]). Operands are stored as planes: plane 0 = bf16(x); in fp32-parity
+// mode plane 1 = bf16(x - plane0), and the K loop runs three segments (A0*B0, A0*B1, A1*B0).
+enum EpiKind : int { EPI_STORE = 0, EPI_ROPE = 1, EPI_GEGLU = 2, EPI_RESID = 3 };
+enum OutMode : int { OUT_BF16 = 0, OUT_BF16X2 = 1, OUT_F32 = 2 };
+enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2 };
+
+struct GemmShape {
+  int M;     // rows of A that are valid (rows beyond are computed from whatever the buffer holds and never stored)
+  int N;     // rows of B (for EPI_GEGLU: 2*I, interleaved in groups of BN/2)
+  int K;     // reduction length of one segment
+  int nseg;  // 1 (bf16) or 3 (split-bf16 fp32 emulation)
+};
+
+struct GemmEpi {
+  int kind = EPI_STORE;
+  int out_mode = OUT_BF16;
+  void* out = nullptr;         // EPI_STORE / EPI_ROPE / EPI_GEGLU output base
+  long long ld = 0;            // output (or residual) row stride in elements
+  long long plane = 0;         // plane stride in elements (OUT_BF16X2)
+  float* resid = nullptr;      // EPI_RESID: fp32 [M, ld], updated in place
+  const float* bias = nullptr; // [N] fp32, optional
+  int act = ACT_NONE;
+  const float* cos_t = nullptr;  // EPI_ROPE: [max_pos, 32] tables for this layer's theta
+  const float* sin_t = nullptr;
+  const int* pos = nullptr;      // EPI_ROPE: position of each row within its sequence
+  int rope_cols = 0;             // EPI_ROPE: rotate columns [0, rope_cols) (q and k), head dim 64
+  int geglu_I = 0;               // EPI_GEGLU: output width I
+};
+
+// Builds a 3-D tensor map {K, rows, planes} over a bf16 operand with a {64, box_rows, 1} box and the
+// 128-byte swizzle. Returns false if the driver rejects it (alignment).
+bool make_operand_map(CUtensorMap* map, const void* base, uint64_t K, uint64_t rows, uint64_t planes,
+                      uint32_t box_rows);
+
+// bn is 128 or 256 and must match the box height of `tb`. `grid_ctas` caps the persistent grid.
+cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, int bn, const GemmShape& sh,
+                        const GemmEpi& ep, int* err, int grid_ctas, cudaStream_t st);
+
+// ------------------------------------------------------------------ attention
+// Work item of the attention kernels: 64 query rows of one sequence.
+struct AttnItem {
+  int seq;   // sequence index within the pass (< 0: unused slot)
+  int q0;    // first query position within the sequence (contiguous mode)
+  int goff;  // gathered mode: offset into the gathered-row lists
+  int nq;    // gathered mode: number of query rows (<= 64)
+};
+struct AttnArgs {
+  const void* qkv;       // [rows, 3*D]: bf16 (fast path) or fp32 (parity path)
+  void* out;             // bf16 planes [P][rows_out, D]
+  long long out_plane;   // plane stride (elements) when P == 2
+  int out_planes;        // 1 or 2
+  const AttnItem* items;
+  int n_items;
+  const int* soff;       // [B] first packed row of each sequence
+  const int* slen;       // [B] sequence length
+  const int* gsrc;       // gathered mode: packed row of each gathered query
+  int gathered;          // 0: contiguous query blocks, 1: gathered queries (full attention)
+  int H;                 // heads (head dim is 64)
+  int window;            // half window (|q-k| <= window), 0 = global
+  float scale;           // softmax scale (1/sqrt(64))
+};
+cudaError_t attn_bf16_launch(const AttnArgs& a, cudaStream_t st);
+cudaError_t attn_f32_launch(const AttnArgs& a, cudaStream_t st);
+
+// ------------------------------------------------------------------ row kernels (LayerNorm family)
+// One warp per row. Source row: emb[ids[r]] (embedding), x[gidx[r]] (gather) or x[r].
+// v = source (+ add_row); y = LN(v) * w (+ b) (+ type_emb[qtype[rowseq[r]]]);
+// optional second LayerNorm z = LN(y) * w2 (+ b2) feeding the bf16 planes.
+struct LnArgs {
+  int rows = 0, D = 0;
+  float eps = 1e-5f;
+  const float* src = nullptr;     // fp32 [*, D]
+  const int* ids = nullptr;       // embedding lookup indices (src = table)
+  const int* gidx = nullptr;      // gather indices
+  const float* w = nullptr;       // LN gain (null: identity LayerNorm skipped, y = v)
+  const float* b = nullptr;
+  const float* type_emb = nullptr;  // [3, D]
+  const int* qtype = nullptr;       // [B]
+  const int* rowseq = nullptr;      // [rows], < 0: padding row (no type embedding)
+  float* copy_f32 = nullptr;      // write v (pre-norm source row) as fp32 [rows, D]
+  float* out_f32 = nullptr;       // write y as fp32 (may alias src when no gather)
+  const float* w2 = nullptr;      // second LayerNorm (optional)
+  const float* b2 = nullptr;
+  bf16* out_bf = nullptr;         // write (second LN ? z : y) as bf16 planes
+  int out_planes = 1;
+  long long out_plane = 0;
+};
+cudaError_t ln_launch(const LnArgs& a, cudaStream_t st);
+
+// ------------------------------------------------------------------ decision-head outputs
+// One CTA per question: marker logits (scorer's final Linear(d,1)), softmax features, act head.
+struct HeadOutArgs {
+  int B = 0, D = 0, n_act = 0;
+  const void* hs = nullptr;       // scorer hidden [KT, D] (GELU output), bf16 or fp32
+  int hs_f32 = 0;
+  const float* w3 = nullptr;      // [D]
+  float b3 = 0.f;
+  const float* cls = nullptr;     // fp32 CLS rows after the head [B, D]
+  const int* moff = nullptr;      // [B] first gathered marker row / logit index of each question
+  const int* nmark = nullptr;     // [B]
+  const float* w0 = nullptr;      // act head Linear(D+4, 256): [256, D+4]
+  const float* b0 = nullptr;
+  const float* w2 = nullptr;      // Linear(256, n_act): [n_act, 256]
+  const float* b2 = nullptr;
+  float* logits = nullptr;        // [sum nmark]
+  float* act = nullptr;           // [B, n_act]
+};
+cudaError_t head_out_launch(const HeadOutArgs& a, cudaStream_t st);
+
+}  // namespace laya
