@@ -66,7 +66,9 @@ WEIGHTS_OF = {"large1024": "large"}
 def param_specs(a: Arch):
     """(name, shape, kind) in DecisionModel.state_dict() order; kind: 'w' N(0,.02), 'g' 1+N(0,.02), 'one'."""
     D, I, V = a.d, a.inter, a.vocab
-    s = [("encoder.embeddings.tok_embeddings.weight", (V, D), "w"), ("encoder.embeddings.norm.weight", (D,), "g")]
+    # DecisionModel's own buffer comes before its submodules in state_dict()
+    s = [("temperature", (3,), "one"), ("encoder.embeddings.tok_embeddings.weight", (V, D), "w"),
+         ("encoder.embeddings.norm.weight", (D,), "g")]
     for i in range(a.layers):
         p = "encoder.layers.%d." % i
         if i > 0:
@@ -86,8 +88,7 @@ def param_specs(a: Arch):
     s += [("type_emb.weight", (3, D), "w"), ("scorer.0.weight", (D,), "g"), ("scorer.0.bias", (D,), "w"),
           ("scorer.1.weight", (D, D), "w"), ("scorer.1.bias", (D,), "w"), ("scorer.3.weight", (1, D), "w"),
           ("scorer.3.bias", (1,), "w"), ("act_head.0.weight", (256, D + 4), "w"), ("act_head.0.bias", (256,), "w"),
-          ("act_head.2.weight", (a.n_act, 256), "w"), ("act_head.2.bias", (a.n_act,), "w"),
-          ("temperature", (3,), "one")]
+          ("act_head.2.weight", (a.n_act, 256), "w"), ("act_head.2.bias", (a.n_act,), "w")]
     return s
 
 
@@ -136,7 +137,7 @@ def checkpoint(arch: str, seed: int = 0, root: str = None) -> str:
     """Returns the directory of the seeded checkpoint for `arch`, generating it on first use."""
     a = ARCHS[arch]
     root = root or default_root()
-    key = hashlib.sha1(json.dumps([asdict(a), seed, 2]).encode()).hexdigest()[:10]
+    key = hashlib.sha1(json.dumps([asdict(a), seed, 3]).encode()).hexdigest()[:10]
     d = os.path.join(root, "%s-s%d-%s" % (arch, seed, key))
     done = os.path.join(d, ".complete")
     if os.path.exists(done):

@@ -1,0 +1,84 @@
+"""Pins the numpy oracle (oracle/model.py) to the reference's own PyTorch path through the golden
+fixtures in tests/golden/ (made by tests/golden/make_golden.py from ref/rl_common.py + transformers).
+
+Tolerances: both sides compute in fp32 on the CPU and differ only in reduction order, so hidden
+states agree to max|a-b|/max|b| < 2e-5 per layer and logits / act logits to 1e-5 absolute (relative
+for the act head, whose logits are larger).
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import model as om
+from oracle import synth
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def rel(a, b):
+    return float(np.abs(np.asarray(a, np.float64) - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def questions_of(g):
+    qs, io, mo = [], 0, 0
+    for L, k, qt in zip(g["lens"], g["nmark"], g["qtypes"]):
+        qs.append({"ids": g["ids"][io:io + L].tolist(), "markers": g["markers"][mo:mo + k].tolist(), "qtype": int(qt)})
+        io += L
+        mo += k
+    return qs
+
+
+def check_fingerprint(weights, name):
+    fp = np.load(os.path.join(GOLD, name))
+    for k in fp.files:
+        v = np.asarray(weights[k], np.float64).ravel()
+        got = np.array([v.sum(), (v * v).sum(), v[0]])
+        assert np.allclose(got, fp[k], rtol=1e-9, atol=1e-9), k
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    ck = synth.checkpoint("tiny", 0)
+    w = synth.load_weights(ck)
+    check_fingerprint(w, "tiny_weights_fp.npz")
+    return om.Oracle(w, synth.load_arch(ck))
+
+
+@pytest.mark.parametrize("case", ["tiny_mixed", "tiny_k1", "tiny_full"])
+def test_tiny_layers(tiny, case):
+    g = np.load(os.path.join(GOLD, case + ".npz"))
+    qs = questions_of(g)
+    lo, ac, caps = tiny.forward_batch(qs, capture=True)
+    assert np.abs(lo - g["logits"]).max() < 1e-5
+    assert np.abs(ac - g["act"]).max() < 1e-5 * max(1.0, np.abs(g["act"]).max())
+    for key in ["emb", "final_norm"] + ["enc%d" % i for i in range(4)] + ["head0", "head1"]:
+        mine = np.concatenate([c[key] for c in caps])
+        assert rel(mine, g["t_" + key]) < 2e-5, key
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("case", ["large_c1", "large_multi"])
+def test_large(case):
+    ck = synth.checkpoint("large", 0)
+    w = synth.load_weights(ck)
+    check_fingerprint(w, "large_weights_fp.npz")
+    o = om.Oracle(w, synth.load_arch(ck))
+    g = np.load(os.path.join(GOLD, case + ".npz"))
+    qs = questions_of(g)
+    lo, ac, caps = o.forward_batch(qs, capture=True)
+    assert np.abs(lo - g["logits"]).max() < 2e-5
+    assert np.abs(ac - g["act"]).max() < 2e-5 * max(1.0, np.abs(g["act"]).max())
+    rows = g["sample_rows"]
+    for key in ["emb", "final_norm", "head0", "head1"] + ["enc%d" % i for i in range(28)]:
+        norms = np.concatenate([np.linalg.norm(c[key], axis=-1) for c in caps])
+        assert rel(norms, g["n_" + key]) < 2e-5, key
+        assert rel(caps[0][key][rows], g["s_" + key]) < 5e-5, key
+
+
+def test_rope_tables_match_transformers_formula():
+    cos, sin = om.rope_tables(8, 10000.0)
+    inv = 1.0 / (10000.0 ** (np.arange(0, 64, 2) / 64))
+    f = np.arange(8)[:, None] * inv[None, :]
+    assert np.abs(cos[:, :32] - np.cos(f)).max() < 1e-6
+    assert np.abs(sin[:, 32:] - np.sin(f)).max() < 1e-6
