@@ -94,6 +94,11 @@ int laya_stage(void* h, int B, const int* lens, const int* ids, const int* nmark
 int laya_replay(void* h, int iters, double* ms);
 int laya_staged_results(void* h, float* logits, float* act);
 
+/* Cumulative counters of the forward and replay calls since the last reset, summed over devices:
+ * kernel launches of this library, bytes copied host->device and device->host. reset != 0 clears
+ * them after reading. */
+int laya_io_stats(void* h, long long* launches, long long* h2d_bytes, long long* d2h_bytes, int reset);
+
 /* Writes the residual stream after the embedding, after every encoder layer (before the final
  * norm), after the final norm + type embedding, and after each head layer for the last forward call
  * when dumping is on: files emb.bin, enc<i>.bin, final.bin, head<i>.bin (fp32, one row per packed

@@ -56,6 +56,8 @@ def load_lib(path: str = LIB_PATH) -> ctypes.CDLL:
         "laya_replay": (i, [vp, i, ctypes.POINTER(d)]),
         "laya_staged_results": (i, [vp, _FP, _FP]),
         "laya_set_dump_dir": (i, [vp, ctypes.c_char_p]),
+        "laya_io_stats": (i, [vp, ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_longlong),
+                              ctypes.POINTER(ctypes.c_longlong), i]),
         "laya_b200_gemm": (i, [vp, vp, vp, vp, vp, i, i, i, i, i, i, i, i, vp, vp, vp, i, i, vp, i]),
     }
     for name, (res, args) in sig.items():

@@ -14,6 +14,7 @@ int* err_word(int dev) {
   std::lock_guard<std::mutex> lk(g_mu);
   if ((int)g_err.size() <= dev) g_err.resize(dev + 1, nullptr);
   if (!g_err[dev]) {
+    if (laya::gemm_prepare_device() != cudaSuccess) return nullptr;
     if (cudaMalloc(&g_err[dev], sizeof(int)) != cudaSuccess) return nullptr;
     cudaMemset(g_err[dev], 0, sizeof(int));
   }

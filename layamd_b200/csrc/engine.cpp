@@ -1,0 +1,1094 @@
+// Laya B200 engine host code; see engine.hpp for the design. Host C++ over the CUDA runtime: no
+// kernel is launched from here directly, only through the launchers of kernels.h.
+#include "engine.hpp"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <numeric>
+#include <thread>
+
+namespace laya {
+
+namespace {
+
+#define LAYA_TRY(expr)                                                                                   \
+  do {                                                                                                   \
+    cudaError_t e_ = (expr);                                                                             \
+    if (e_ != cudaSuccess) {                                                                             \
+      if (err) *err = std::string(#expr) + ": " + cudaGetErrorString(e_);                                \
+      return false;                                                                                      \
+    }                                                                                                    \
+  } while (0)
+
+uint16_t f32_to_bf16(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fc0;  // NaN
+  u += 0x7fffu + ((u >> 16) & 1u);                     // round to nearest even
+  return static_cast<uint16_t>(u >> 16);
+}
+float bf16_to_f32(uint16_t h) {
+  const uint32_t u = static_cast<uint32_t>(h) << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+int env_int(const char* k, int d) {
+  const char* v = getenv(k);
+  return v && *v ? atoi(v) : d;
+}
+
+size_t align4(size_t n) { return (n + 3) & ~size_t(3); }
+
+// Offsets (in ints) of the per-pass metadata arrays inside the staging block.
+struct MetaLayout {
+  size_t ids, pos, rowseq, soff, slen, qt, nm, moff, items, gitems, gsrc, gdst, grow, total;
+  int items_cap, gitems_cap;
+};
+MetaLayout meta_layout(int Tpad, int n, int R) {
+  MetaLayout L;
+  size_t o = 0;
+  auto take = [&](size_t cnt) { size_t r = o; o += align4(cnt); return r; };
+  L.items_cap = Tpad / 64 + n;
+  L.gitems_cap = R / 64 + n + 1;
+  L.ids = take(Tpad);
+  L.pos = take(Tpad);
+  L.rowseq = take(Tpad);
+  L.soff = take(n);
+  L.slen = take(n);
+  L.qt = take(n);
+  L.nm = take(n);
+  L.moff = take(n);
+  L.items = take((size_t)L.items_cap * 4);
+  L.gitems = take((size_t)L.gitems_cap * 4);
+  L.gsrc = take(R);
+  L.gdst = take(R);
+  L.grow = take(R);
+  L.total = o;
+  return L;
+}
+
+}  // namespace
+
+bool validate_batch(int B, const int* lens, const int* nmark, const int* markers, int max_len) {
+  if (B < 0) return false;
+  size_t mo = 0;
+  for (int b = 0; b < B; ++b) {
+    if (lens[b] < 1 || lens[b] > max_len || nmark[b] < 1 || nmark[b] > kMaxMarkers) return false;
+    for (int k = 0; k < nmark[b]; ++k)
+      if (markers[mo + k] < 0 || markers[mo + k] >= lens[b]) return false;
+    mo += nmark[b];
+  }
+  return true;
+}
+
+bool plan_passes(int B, const int* lens, const int* nmark, int pass_tokens, int max_seqs, int max_gathered,
+                 std::vector<PassPlan>* out) {
+  out->clear();
+  int b0 = 0;
+  while (b0 < B) {
+    PassPlan p;
+    p.b0 = b0;
+    while (b0 + p.n < B && p.n < max_seqs) {
+      const int b = b0 + p.n;
+      if (p.n > 0 && (p.T + lens[b] > pass_tokens || p.KT + nmark[b] + p.n + 1 > max_gathered)) break;
+      if (p.n == 0 && (lens[b] > pass_tokens || nmark[b] + 1 > max_gathered)) return false;
+      p.T += lens[b];
+      p.KT += nmark[b];
+      ++p.n;
+    }
+    p.Tpad = (p.T + 63) / 64 * 64;
+    p.R = p.KT + p.n;
+    out->push_back(p);
+    b0 += p.n;
+  }
+  return true;
+}
+
+// ===================================================================== Replica (one GPU)
+class Replica {
+ public:
+  Engine& E;
+  const Config& cfg;
+  int dev = 0, P = 1, nseg = 1, num_sms = 148;
+  cudaStream_t st = nullptr;
+  std::vector<void*> allocs;
+  std::vector<void*> host_allocs;
+
+  // weights
+  float *tok_emb = nullptr, *emb_norm = nullptr, *final_norm = nullptr, *type_emb = nullptr;
+  struct Layer {
+    float* attn_norm = nullptr;
+    float* mlp_norm = nullptr;
+    Mat Wqkv, Wo, Wi, Wmo;
+  };
+  struct Head {
+    float *n1w, *n1b, *n2w, *n2b, *inB, *outB, *l1B, *l2B;
+    Mat inW, outW, l1W, l2W;
+  };
+  std::vector<Layer> enc;
+  std::vector<Head> head;
+  Mat sc1;
+  float *sc_nw = nullptr, *sc_nb = nullptr, *sc1B = nullptr, *sc3W = nullptr;
+  float sc3B = 0.f;
+  float *a0W = nullptr, *a0B = nullptr, *a2W = nullptr, *a2B = nullptr;
+  float *cos_g = nullptr, *sin_g = nullptr, *cos_l = nullptr, *sin_l = nullptr;
+
+  // activations
+  int Tcap = 0, Rcap = 0, Bcap = 0;
+  float* x = nullptr;
+  void* qkv = nullptr;
+  Operand xn, ao, mg, ff, xng, aog, ffg, xs;
+  float* xg = nullptr;
+  void* hs = nullptr;
+  float *d_logits = nullptr, *d_act = nullptr;
+  int* d_err = nullptr;
+
+  // per-pass staging
+  int* h_meta = nullptr;
+  int* d_meta = nullptr;
+  size_t meta_cap = 0;
+  float* h_out = nullptr;  // logits [Rcap] | act [Bcap * n_act] | err
+
+  // graphs
+  std::map<std::tuple<int, int, int, int>, cudaGraphExec_t> graphs;
+  bool capturing = false;
+
+  // profiling: per stage (device ms, launches)
+  std::vector<std::pair<std::string, std::pair<double, long long>>> prof_acc;
+  std::vector<std::tuple<const char*, cudaEvent_t, cudaEvent_t>> prof_pending;
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
+
+  // staged pass (benchmark replay)
+  std::vector<Question> staged;
+  PassPlan staged_plan;
+  cudaGraphExec_t staged_graph = nullptr;
+
+  Replica(Engine& e, int d) : E(e), cfg(e.cfg), dev(d) {}
+  ~Replica() { release(); }
+
+  void release() {
+    cudaSetDevice(dev);
+    if (st) cudaStreamSynchronize(st);
+    for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+    graphs.clear();
+    if (staged_graph) cudaGraphExecDestroy(staged_graph);
+    staged_graph = nullptr;
+    for (auto ev : ev_pool) cudaEventDestroy(ev);
+    ev_pool.clear();
+    for (void* p : allocs) cudaFree(p);
+    allocs.clear();
+    for (void* p : host_allocs) cudaFreeHost(p);
+    host_allocs.clear();
+    if (st) cudaStreamDestroy(st);
+    st = nullptr;
+  }
+
+  template <typename T>
+  bool dalloc(T** p, size_t bytes, std::string* err) {
+    void* q = nullptr;
+    LAYA_TRY(cudaMalloc(&q, bytes < 16 ? 16 : bytes));
+    LAYA_TRY(cudaMemset(q, 0, bytes < 16 ? 16 : bytes));
+    allocs.push_back(q);
+    *p = static_cast<T*>(q);
+    return true;
+  }
+
+  bool upload_vec(const SafeTensors& st_, const std::string& name, float** out, std::string* err, size_t expect = 0) {
+    std::vector<float> v;
+    if (!st_.to_f32(name, &v, err)) return false;
+    if (expect && v.size() != expect) { *err = name + ": unexpected size"; return false; }
+    if (!dalloc(out, v.size() * 4, err)) return false;
+    LAYA_TRY(cudaMemcpy(*out, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+    return true;
+  }
+
+  // [N, K] weight -> P bf16 planes (hi, and lo = bf16(w - hi) in parity mode), optionally with the
+  // GeGLU row interleave: groups of 64 input rows followed by their 64 gate rows.
+  bool upload_mat(const SafeTensors& st_, const std::string& name, int N, int K, Mat* m, std::string* err,
+                  bool geglu = false) {
+    std::vector<float> v;
+    if (!st_.to_f32(name, &v, err)) return false;
+    if (v.size() != (size_t)N * K) { *err = name + ": unexpected shape"; return false; }
+    if (geglu) {
+      const int I = N / 2;
+      std::vector<float> w(v.size());
+      int r = 0;
+      for (int j = 0; j < I; j += 64) {
+        for (int i = 0; i < 64; ++i, ++r) memcpy(&w[(size_t)r * K], &v[(size_t)(j + i) * K], (size_t)K * 4);
+        for (int i = 0; i < 64; ++i, ++r) memcpy(&w[(size_t)r * K], &v[(size_t)(I + j + i) * K], (size_t)K * 4);
+      }
+      v.swap(w);
+    }
+    std::vector<uint16_t> h((size_t)P * N * K);
+    for (size_t i = 0; i < v.size(); ++i) {
+      const uint16_t hi = f32_to_bf16(v[i]);
+      h[i] = hi;
+      if (P == 2) h[v.size() + i] = f32_to_bf16(v[i] - bf16_to_f32(hi));
+    }
+    if (!dalloc(&m->p, h.size() * 2, err)) return false;
+    LAYA_TRY(cudaMemcpy(m->p, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
+    m->N = N;
+    m->K = K;
+    if (!make_operand_map(&m->m128, m->p, K, N, P, 128)) { *err = name + ": tensor map rejected"; return false; }
+    if (N >= 256 && !make_operand_map(&m->m256, m->p, K, N, P, 256)) {
+      *err = name + ": tensor map rejected";
+      return false;
+    }
+    return true;
+  }
+
+  bool make_operand(Operand* op, int rows, int K, std::string* err) {
+    op->rows = rows;
+    op->K = K;
+    op->plane = (long long)rows * K;
+    if (!dalloc(&op->p, (size_t)P * rows * K * 2, err)) return false;
+    if (!make_operand_map(&op->map, op->p, K, rows, P, 128)) { *err = "activation tensor map rejected"; return false; }
+    return true;
+  }
+
+  bool load(const SafeTensors& W, std::string* err) {
+    LAYA_TRY(cudaSetDevice(dev));
+    LAYA_TRY(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev));
+    LAYA_TRY(gemm_prepare_device());
+    LAYA_TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    P = E.precision == 1 ? 2 : 1;
+    nseg = P == 2 ? 3 : 1;
+    const int D = cfg.d, I = cfg.intermediate, FF = cfg.head_ffn, V = cfg.vocab;
+    if (!upload_vec(W, "encoder.embeddings.tok_embeddings.weight", &tok_emb, err, (size_t)V * D)) return false;
+    if (!upload_vec(W, "encoder.embeddings.norm.weight", &emb_norm, err, D)) return false;
+    if (!upload_vec(W, "encoder.final_norm.weight", &final_norm, err, D)) return false;
+    if (!upload_vec(W, "type_emb.weight", &type_emb, err, (size_t)3 * D)) return false;
+    enc.resize(cfg.n_layers);
+    char b[160];
+    for (int i = 0; i < cfg.n_layers; ++i) {
+      auto T = [&](const char* f) { snprintf(b, sizeof b, f, i); return std::string(b); };
+      if (W.get(T("encoder.layers.%d.attn_norm.weight"))) {
+        if (!upload_vec(W, T("encoder.layers.%d.attn_norm.weight"), &enc[i].attn_norm, err, D)) return false;
+      }
+      if (!upload_mat(W, T("encoder.layers.%d.attn.Wqkv.weight"), 3 * D, D, &enc[i].Wqkv, err)) return false;
+      if (!upload_mat(W, T("encoder.layers.%d.attn.Wo.weight"), D, D, &enc[i].Wo, err)) return false;
+      if (!upload_vec(W, T("encoder.layers.%d.mlp_norm.weight"), &enc[i].mlp_norm, err, D)) return false;
+      if (!upload_mat(W, T("encoder.layers.%d.mlp.Wi.weight"), 2 * I, D, &enc[i].Wi, err, true)) return false;
+      if (!upload_mat(W, T("encoder.layers.%d.mlp.Wo.weight"), D, I, &enc[i].Wmo, err)) return false;
+    }
+    head.resize(cfg.head_layers);
+    for (int j = 0; j < cfg.head_layers; ++j) {
+      auto T = [&](const char* f) { snprintf(b, sizeof b, f, j); return std::string(b); };
+      Head& h = head[j];
+      if (!upload_vec(W, T("head.layers.%d.norm1.weight"), &h.n1w, err, D) ||
+          !upload_vec(W, T("head.layers.%d.norm1.bias"), &h.n1b, err, D) ||
+          !upload_vec(W, T("head.layers.%d.norm2.weight"), &h.n2w, err, D) ||
+          !upload_vec(W, T("head.layers.%d.norm2.bias"), &h.n2b, err, D) ||
+          !upload_mat(W, T("head.layers.%d.self_attn.in_proj_weight"), 3 * D, D, &h.inW, err) ||
+          !upload_vec(W, T("head.layers.%d.self_attn.in_proj_bias"), &h.inB, err, 3 * D) ||
+          !upload_mat(W, T("head.layers.%d.self_attn.out_proj.weight"), D, D, &h.outW, err) ||
+          !upload_vec(W, T("head.layers.%d.self_attn.out_proj.bias"), &h.outB, err, D) ||
+          !upload_mat(W, T("head.layers.%d.linear1.weight"), FF, D, &h.l1W, err) ||
+          !upload_vec(W, T("head.layers.%d.linear1.bias"), &h.l1B, err, FF) ||
+          !upload_mat(W, T("head.layers.%d.linear2.weight"), D, FF, &h.l2W, err) ||
+          !upload_vec(W, T("head.layers.%d.linear2.bias"), &h.l2B, err, D))
+        return false;
+    }
+    if (!upload_vec(W, "scorer.0.weight", &sc_nw, err, D) || !upload_vec(W, "scorer.0.bias", &sc_nb, err, D) ||
+        !upload_mat(W, "scorer.1.weight", D, D, &sc1, err) || !upload_vec(W, "scorer.1.bias", &sc1B, err, D) ||
+        !upload_vec(W, "scorer.3.weight", &sc3W, err, D))
+      return false;
+    {
+      std::vector<float> v;
+      if (!W.to_f32("scorer.3.bias", &v, err)) return false;
+      sc3B = v.at(0);
+    }
+    if (!upload_vec(W, "act_head.0.weight", &a0W, err, (size_t)256 * (D + 4)) ||
+        !upload_vec(W, "act_head.0.bias", &a0B, err, 256) ||
+        !upload_vec(W, "act_head.2.weight", &a2W, err, (size_t)cfg.n_act * 256) ||
+        !upload_vec(W, "act_head.2.bias", &a2B, err, cfg.n_act))
+      return false;
+    if (!rope_tables(err)) return false;
+    return alloc_arena(err);
+  }
+
+  // cos/sin [max_len, 32] per theta as transformers computes them: inv_freq = 1/theta^(2i/64) and
+  // the angle pos*inv_freq in fp32, then cos/sin of that fp32 angle.
+  bool rope_tables(std::string* err) {
+    const int L = cfg.max_len, H2 = cfg.head_dim / 2;
+    std::vector<float> cg((size_t)L * H2), sg(cg.size()), cl(cg.size()), sl(cg.size());
+    for (int i = 0; i < H2; ++i) {
+      const float e = static_cast<float>(2 * i) / static_cast<float>(cfg.head_dim);
+      const float ig = 1.0f / static_cast<float>(std::pow((double)cfg.rope_theta_global, (double)e));
+      const float il = 1.0f / static_cast<float>(std::pow((double)cfg.rope_theta_local, (double)e));
+      for (int p = 0; p < L; ++p) {
+        const float fg = static_cast<float>(p) * ig, fl = static_cast<float>(p) * il;
+        cg[(size_t)p * H2 + i] = static_cast<float>(std::cos((double)fg));
+        sg[(size_t)p * H2 + i] = static_cast<float>(std::sin((double)fg));
+        cl[(size_t)p * H2 + i] = static_cast<float>(std::cos((double)fl));
+        sl[(size_t)p * H2 + i] = static_cast<float>(std::sin((double)fl));
+      }
+    }
+    for (auto pr : {std::make_pair(&cos_g, &cg), std::make_pair(&sin_g, &sg), std::make_pair(&cos_l, &cl),
+                    std::make_pair(&sin_l, &sl)}) {
+      if (!dalloc(pr.first, pr.second->size() * 4, err)) return false;
+      LAYA_TRY(cudaMemcpy(*pr.first, pr.second->data(), pr.second->size() * 4, cudaMemcpyHostToDevice));
+    }
+    return true;
+  }
+
+  bool alloc_arena(std::string* err) {
+    const int D = cfg.d, I = cfg.intermediate, FF = cfg.head_ffn;
+    Tcap = (E.max_tokens + 63) / 64 * 64;
+    Rcap = E.max_gathered;
+    Bcap = E.max_seqs;
+    if (!dalloc(&x, (size_t)Tcap * D * 4, err)) return false;
+    const size_t qkv_bytes = (size_t)Tcap * 3 * D * (P == 2 ? 4 : 2);
+    if (!dalloc(reinterpret_cast<char**>(&qkv), qkv_bytes, err)) return false;
+    if (!make_operand(&xn, Tcap, D, err) || !make_operand(&ao, Tcap, D, err) || !make_operand(&mg, Tcap, I, err) ||
+        !make_operand(&ff, Tcap, FF, err) || !make_operand(&xng, Rcap, D, err) || !make_operand(&aog, Rcap, D, err) ||
+        !make_operand(&ffg, Rcap, FF, err) || !make_operand(&xs, Rcap, D, err))
+      return false;
+    if (!dalloc(&xg, (size_t)Rcap * D * 4, err)) return false;
+    if (!dalloc(reinterpret_cast<char**>(&hs), (size_t)Rcap * D * (P == 2 ? 4 : 2), err)) return false;
+    if (!dalloc(&d_logits, (size_t)Rcap * 4, err)) return false;
+    if (!dalloc(&d_act, (size_t)Bcap * cfg.n_act * 4, err)) return false;
+    if (!dalloc(&d_err, 16, err)) return false;
+    const MetaLayout L = meta_layout(Tcap, Bcap, Rcap);
+    meta_cap = L.total;
+    if (!dalloc(&d_meta, meta_cap * 4, err)) return false;
+    void* hp = nullptr;
+    LAYA_TRY(cudaMallocHost(&hp, meta_cap * 4));
+    host_allocs.push_back(hp);
+    h_meta = static_cast<int*>(hp);
+    LAYA_TRY(cudaMallocHost(&hp, ((size_t)Rcap + (size_t)Bcap * cfg.n_act + 4) * 4));
+    host_allocs.push_back(hp);
+    h_out = static_cast<float*>(hp);
+    return true;
+  }
+
+  // ------------------------------------------------------------------ one pass
+  // Fills the pinned staging block for pass `p` of `qs`.
+  void fill(const PassPlan& p, const Question* qs) {
+    const MetaLayout L = meta_layout(p.Tpad, p.n, p.R);
+    int* m = h_meta;
+    AttnItem* items = reinterpret_cast<AttnItem*>(m + L.items);
+    AttnItem* gitems = reinterpret_cast<AttnItem*>(m + L.gitems);
+    int r = 0, mo = 0, it = 0, git = 0, gl = 0;
+    for (int i = 0; i < p.n; ++i) {
+      const Question& q = qs[p.b0 + i];
+      m[L.soff + i] = r;
+      m[L.slen + i] = q.len;
+      m[L.qt + i] = q.qtype;
+      m[L.nm + i] = q.nmark;
+      m[L.moff + i] = mo;
+      memcpy(m + L.ids + r, q.ids, (size_t)q.len * 4);
+      for (int j = 0; j < q.len; ++j) {
+        m[L.pos + r + j] = j;
+        m[L.rowseq + r + j] = i;
+      }
+      for (int q0 = 0; q0 < q.len; q0 += 64) items[it++] = AttnItem{i, q0, 0, 0};
+      const int cnt = q.nmark + 1;
+      for (int k = 0; k < q.nmark; ++k) {
+        m[L.gsrc + gl + k] = r + q.markers[k];
+        m[L.gdst + gl + k] = mo + k;
+        m[L.grow + mo + k] = r + q.markers[k];
+      }
+      m[L.gsrc + gl + q.nmark] = r;
+      m[L.gdst + gl + q.nmark] = p.KT + i;
+      m[L.grow + p.KT + i] = r;
+      for (int c0 = 0; c0 < cnt; c0 += 64) gitems[git++] = AttnItem{i, 0, gl + c0, std::min(64, cnt - c0)};
+      gl += cnt;
+      r += q.len;
+      mo += q.nmark;
+    }
+    for (int j = r; j < p.Tpad; ++j) {
+      m[L.ids + j] = cfg.pad_id;
+      m[L.pos + j] = 0;
+      m[L.rowseq + j] = -1;
+    }
+    for (; it < L.items_cap; ++it) items[it] = AttnItem{-1, 0, 0, 0};
+    for (; git < L.gitems_cap; ++git) gitems[git] = AttnItem{-1, 0, 0, 0};
+  }
+
+  cudaError_t first_err = cudaSuccess;
+  void chk(cudaError_t e) {
+    if (e != cudaSuccess && first_err == cudaSuccess) first_err = e;
+  }
+  // kernel launches of the pass being enqueued, and cumulative I/O counters (laya_io_stats)
+  int pass_launches = 0;
+  long long n_launches = 0, n_h2d = 0, n_d2h = 0;
+  std::map<std::tuple<int, int, int, int>, int> graph_launches;
+  int staged_launches = 0;
+  void launched(cudaError_t e) {
+    chk(e);
+    ++pass_launches;
+  }
+  void count_pass(const PassPlan& p, int launches) {
+    n_launches += launches;
+    n_h2d += (long long)meta_layout(p.Tpad, p.n, p.R).total * 4;
+    n_d2h += (long long)p.KT * 4 + (long long)p.n * cfg.n_act * 4 + 4;
+  }
+  cudaEvent_t take_event() {
+    if (ev_used == ev_pool.size()) {
+      cudaEvent_t ev;
+      cudaEventCreate(&ev);
+      ev_pool.push_back(ev);
+    }
+    return ev_pool[ev_used++];
+  }
+  template <typename F>
+  void stage(const char* name, F&& fn) {
+    const bool timed = E.prof_on && !capturing;
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (timed) {
+      a = take_event();
+      b = take_event();
+      cudaEventRecord(a, st);
+    }
+    fn();
+    if (timed) {
+      cudaEventRecord(b, st);
+      prof_pending.emplace_back(name, a, b);
+    }
+  }
+  void prof_collect() {
+    for (auto& t : prof_pending) {
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, std::get<1>(t), std::get<2>(t));
+      const std::string n = std::get<0>(t);
+      bool found = false;
+      for (auto& kv : prof_acc)
+        if (kv.first == n) { kv.second.first += ms; kv.second.second += 1; found = true; break; }
+      if (!found) prof_acc.push_back({n, {(double)ms, 1}});
+    }
+    prof_pending.clear();
+    ev_used = 0;
+  }
+
+  int pick_bn(int M, const Mat& W) const {
+    if (W.N < 256) return 128;
+    const long long t256 = (long long)((M + 127) / 128) * ((W.N + 255) / 256);
+    return t256 >= 2LL * num_sms ? 256 : 128;
+  }
+  void gemm(const Operand& A, int M, const Mat& W, const GemmEpi& ep) {
+    const int bn = pick_bn(M, W);
+    GemmShape sh{M, W.N, W.K, nseg};
+    launched(gemm_launch(A.map, bn == 256 ? W.m256 : W.m128, bn, sh, ep, d_err, num_sms, st));
+  }
+  GemmEpi epi_store(void* out, long long ld, long long plane, int out_mode, const float* bias, int act) const {
+    GemmEpi e;
+    e.kind = EPI_STORE;
+    e.out = out;
+    e.ld = ld;
+    e.plane = plane;
+    e.out_mode = out_mode;
+    e.bias = bias;
+    e.act = act;
+    return e;
+  }
+  GemmEpi epi_resid(float* xres, long long ld, const float* bias) const {
+    GemmEpi e;
+    e.kind = EPI_RESID;
+    e.resid = xres;
+    e.ld = ld;
+    e.bias = bias;
+    return e;
+  }
+  int act_mode() const { return P == 2 ? OUT_BF16X2 : OUT_BF16; }
+  LnArgs ln_base(int rows) const {
+    LnArgs a;
+    a.rows = rows;
+    a.D = cfg.d;
+    a.eps = cfg.norm_eps;
+    a.out_planes = P;
+    return a;
+  }
+  void attend(const AttnItem* items, int n_items, const int* soff, const int* slen, int window, void* out,
+              long long out_plane, const int* gsrc, const int* gdst) {
+    AttnArgs a;
+    a.qkv = qkv;
+    a.out = out;
+    a.out_plane = out_plane;
+    a.out_planes = P;
+    a.items = items;
+    a.n_items = n_items;
+    a.soff = soff;
+    a.slen = slen;
+    a.gsrc = gsrc;
+    a.gdst = gdst;
+    a.gathered = gsrc != nullptr;
+    a.H = cfg.d / 64;
+    a.window = window;
+    a.scale = 0.125f;  // 1/sqrt(64)
+    launched(P == 2 ? attn_f32_launch(a, st) : attn_bf16_launch(a, st));
+  }
+
+  bool dumping() const { return !E.dump_dir.empty() && !capturing && dev == E.reps[0]->dev; }
+  void dump(const char* name, const float* src, int rows) {
+    if (!dumping()) return;
+    std::vector<float> h((size_t)rows * cfg.d);
+    chk(cudaStreamSynchronize(st));
+    chk(cudaMemcpy(h.data(), src, h.size() * 4, cudaMemcpyDeviceToHost));
+    const std::string fn = E.dump_dir + "/" + name + ".bin";
+    if (FILE* f = fopen(fn.c_str(), "wb")) {
+      fwrite(h.data(), 4, h.size(), f);
+      fclose(f);
+    }
+  }
+
+  // Enqueues one pass on the stream: metadata upload (h2d), every kernel, result download (d2h).
+  void enqueue(const PassPlan& p, bool h2d, bool d2h) {
+    const int D = cfg.d, I = cfg.intermediate, FF = cfg.head_ffn, NL = cfg.n_layers, HL = cfg.head_layers;
+    const int M = p.Tpad, R = p.R, KT = p.KT;
+    const MetaLayout L = meta_layout(p.Tpad, p.n, p.R);
+    const int* dm = d_meta;
+    const int *ids = dm + L.ids, *pos = dm + L.pos, *rowseq = dm + L.rowseq, *soff = dm + L.soff,
+              *slen = dm + L.slen, *qt = dm + L.qt, *nm = dm + L.nm, *moff = dm + L.moff, *gsrc = dm + L.gsrc,
+              *gdst = dm + L.gdst, *grow = dm + L.grow;
+    const AttnItem* items = reinterpret_cast<const AttnItem*>(dm + L.items);
+    const AttnItem* gitems = reinterpret_cast<const AttnItem*>(dm + L.gitems);
+    const int qkv_mode = P == 2 ? OUT_F32 : OUT_BF16;
+    char nb[32];
+    if (h2d) stage("h2d", [&] { chk(cudaMemcpyAsync(d_meta, h_meta, L.total * 4, cudaMemcpyHostToDevice, st)); });
+
+    stage("embed_ln", [&] {
+      LnArgs a = ln_base(M);
+      a.src = tok_emb;
+      a.ids = ids;
+      a.w = emb_norm;
+      a.out_f32 = x;
+      a.out_bf = xn.p;
+      a.out_plane = xn.plane;
+      a.w2 = enc[0].attn_norm;  // layer 0 of ModernBERT has no attn_norm (Identity)
+      a.eps2 = cfg.norm_eps;
+      launched(ln_launch(a, st));
+    });
+    dump("emb", x, p.T);
+    for (int l = 0; l < NL; ++l) {
+      const bool glob = cfg.layer_types[l] == AttnKind::Global;
+      stage("gemm_qkv", [&] {
+        GemmEpi e = epi_store(qkv, 3LL * D, 0, qkv_mode, nullptr, ACT_NONE);
+        e.kind = EPI_ROPE;
+        e.cos_t = glob ? cos_g : cos_l;
+        e.sin_t = glob ? sin_g : sin_l;
+        e.pos = pos;
+        e.rope_cols = 2 * D;
+        gemm(xn, M, enc[l].Wqkv, e);
+      });
+      stage(glob ? "attn_global" : "attn_sliding", [&] {
+        attend(items, L.items_cap, soff, slen, glob ? 0 : cfg.local_attention / 2, ao.p, ao.plane, nullptr, nullptr);
+      });
+      stage("gemm_attn_out", [&] { gemm(ao, M, enc[l].Wo, epi_resid(x, D, nullptr)); });
+      stage("ln", [&] {
+        LnArgs a = ln_base(M);
+        a.src = x;
+        a.w = enc[l].mlp_norm;
+        a.out_bf = xn.p;
+        a.out_plane = xn.plane;
+        launched(ln_launch(a, st));
+      });
+      stage("gemm_mlp_in", [&] {
+        GemmEpi e = epi_store(mg.p, I, mg.plane, act_mode(), nullptr, ACT_NONE);
+        e.kind = EPI_GEGLU;
+        e.geglu_I = I;
+        gemm(xn, M, enc[l].Wi, e);
+      });
+      stage("gemm_mlp_out", [&] { gemm(mg, M, enc[l].Wmo, epi_resid(x, D, nullptr)); });
+      snprintf(nb, sizeof nb, "enc%d", l);
+      dump(nb, x, p.T);
+      stage("ln", [&] {
+        LnArgs a = ln_base(M);
+        a.src = x;
+        a.out_bf = xn.p;
+        a.out_plane = xn.plane;
+        if (l + 1 < NL) {
+          a.w = enc[l + 1].attn_norm;
+        } else {  // final norm + type embedding back into x, then the first head layer's norm1
+          a.w = final_norm;
+          a.type_emb = type_emb;
+          a.qtype = qt;
+          a.rowseq = rowseq;
+          a.out_f32 = x;
+          a.w2 = head[0].n1w;
+          a.b2 = head[0].n1b;
+          a.eps2 = 1e-5f;  // nn.TransformerEncoderLayer default layer_norm_eps
+        }
+        launched(ln_launch(a, st));
+      });
+    }
+    dump("final", x, p.T);
+    for (int j = 0; j < HL; ++j) {
+      const Head& h = head[j];
+      const bool last = j == HL - 1;
+      stage("head_gemm", [&] { gemm(xn, M, h.inW, epi_store(qkv, 3LL * D, 0, qkv_mode, h.inB, ACT_NONE)); });
+      if (!last) {
+        stage("head_attn", [&] { attend(items, L.items_cap, soff, slen, 0, ao.p, ao.plane, nullptr, nullptr); });
+        stage("head_gemm", [&] { gemm(ao, M, h.outW, epi_resid(x, D, h.outB)); });
+        stage("head_ln", [&] {
+          LnArgs a = ln_base(M);
+          a.eps = 1e-5f;
+          a.src = x;
+          a.w = h.n2w;
+          a.b = h.n2b;
+          a.out_bf = xn.p;
+          a.out_plane = xn.plane;
+          launched(ln_launch(a, st));
+        });
+        stage("head_gemm", [&] { gemm(xn, M, h.l1W, epi_store(ff.p, FF, ff.plane, act_mode(), h.l1B, ACT_RELU)); });
+        stage("head_gemm", [&] { gemm(ff, M, h.l2W, epi_resid(x, D, h.l2B)); });
+        stage("head_ln", [&] {
+          LnArgs a = ln_base(M);
+          a.eps = 1e-5f;
+          a.src = x;
+          a.w = head[j + 1].n1w;
+          a.b = head[j + 1].n1b;
+          a.out_bf = xn.p;
+          a.out_plane = xn.plane;
+          launched(ln_launch(a, st));
+        });
+        snprintf(nb, sizeof nb, "head%d", j);
+        dump(nb, x, p.T);
+      } else {
+        // only the option-marker rows and the CLS rows are read after the last head layer
+        stage("head_attn", [&] { attend(gitems, L.gitems_cap, soff, slen, 0, aog.p, aog.plane, gsrc, gdst); });
+        stage("head_ln", [&] {
+          LnArgs a = ln_base(R);
+          a.src = x;
+          a.gidx = grow;
+          a.out_f32 = xg;
+          launched(ln_launch(a, st));
+        });
+        stage("head_gemm", [&] { gemm(aog, R, h.outW, epi_resid(xg, D, h.outB)); });
+        stage("head_ln", [&] {
+          LnArgs a = ln_base(R);
+          a.eps = 1e-5f;
+          a.src = xg;
+          a.w = h.n2w;
+          a.b = h.n2b;
+          a.out_bf = xng.p;
+          a.out_plane = xng.plane;
+          launched(ln_launch(a, st));
+        });
+        stage("head_gemm", [&] { gemm(xng, R, h.l1W, epi_store(ffg.p, FF, ffg.plane, act_mode(), h.l1B, ACT_RELU)); });
+        stage("head_gemm", [&] { gemm(ffg, R, h.l2W, epi_resid(xg, D, h.l2B)); });
+        snprintf(nb, sizeof nb, "head%d", j);
+        dump(nb, xg, R);
+      }
+    }
+    stage("scorer", [&] {
+      LnArgs a = ln_base(KT);
+      a.src = xg;
+      a.w = sc_nw;
+      a.b = sc_nb;
+      a.eps = 1e-5f;
+      a.out_bf = xs.p;
+      a.out_plane = xs.plane;
+      launched(ln_launch(a, st));
+      gemm(xs, KT, sc1, epi_store(hs, D, 0, P == 2 ? OUT_F32 : OUT_BF16, sc1B, ACT_GELU));
+    });
+    stage("head_out", [&] {
+      HeadOutArgs a;
+      a.B = p.n;
+      a.D = D;
+      a.n_act = cfg.n_act;
+      a.hs = hs;
+      a.hs_f32 = P == 2;
+      a.w3 = sc3W;
+      a.b3 = sc3B;
+      a.cls = xg + (size_t)KT * D;
+      a.moff = moff;
+      a.nmark = nm;
+      a.w0 = a0W;
+      a.b0 = a0B;
+      a.w2 = a2W;
+      a.b2 = a2B;
+      a.logits = d_logits;
+      a.act = d_act;
+      launched(head_out_launch(a, st));
+    });
+    if (d2h) {
+      stage("d2h", [&] {
+        chk(cudaMemcpyAsync(h_out, d_logits, (size_t)KT * 4, cudaMemcpyDeviceToHost, st));
+        chk(cudaMemcpyAsync(h_out + Rcap, d_act, (size_t)p.n * cfg.n_act * 4, cudaMemcpyDeviceToHost, st));
+        chk(cudaMemcpyAsync(h_out + Rcap + (size_t)Bcap * cfg.n_act, d_err, 4, cudaMemcpyDeviceToHost, st));
+      });
+    }
+  }
+
+  // Runs one pass (graph replay when possible) and leaves its results in h_out. Returns 0 or -2.
+  int execute(const PassPlan& p) {
+    first_err = cudaSuccess;
+    const bool graphs_ok = E.use_graphs && !E.prof_on && E.dump_dir.empty();
+    const auto key = std::make_tuple(p.Tpad, p.n, p.R, p.KT);
+    bool done = false;
+    if (graphs_ok) {
+      auto it = graphs.find(key);
+      if (it == graphs.end() && graphs.size() < 512) {
+        cudaGraph_t g = nullptr;
+        cudaGraphExec_t ex = nullptr;
+        if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+          capturing = true;
+          pass_launches = 0;
+          enqueue(p, true, true);
+          capturing = false;
+          const cudaError_t ce = cudaStreamEndCapture(st, &g);
+          if (ce == cudaSuccess && first_err == cudaSuccess && cudaGraphInstantiate(&ex, g, 0) == cudaSuccess) {
+            it = graphs.emplace(key, ex).first;
+            graph_launches[key] = pass_launches;
+          } else {
+            fprintf(stderr, "[laya] graph capture failed (%s); continuing without graphs\n",
+                    cudaGetErrorString(first_err != cudaSuccess ? first_err : ce));
+            (void)cudaGetLastError();
+            E.use_graphs = false;
+            first_err = cudaSuccess;
+          }
+          if (g) cudaGraphDestroy(g);
+        }
+      }
+      if (it != graphs.end()) {
+        chk(cudaGraphLaunch(it->second, st));
+        count_pass(p, graph_launches[key]);
+        done = true;
+      }
+    }
+    if (!done) {
+      pass_launches = 0;
+      enqueue(p, true, true);
+      count_pass(p, pass_launches);
+    }
+    chk(cudaStreamSynchronize(st));
+    if (E.prof_on) prof_collect();
+    int* herr = reinterpret_cast<int*>(h_out + Rcap + (size_t)Bcap * cfg.n_act);
+    if (first_err != cudaSuccess || *herr != 0) {
+      fprintf(stderr, "[laya] device %d: pass failed (%s, kernel code %d)\n", dev, cudaGetErrorString(first_err),
+              *herr);
+      if (*herr) {
+        int zero = 0;
+        cudaMemcpy(d_err, &zero, 4, cudaMemcpyHostToDevice);
+        *herr = 0;
+      }
+      (void)cudaGetLastError();
+      return -2;
+    }
+    return 0;
+  }
+
+  void scatter(const PassPlan& p, const Question* qs) {
+    const MetaLayout L = meta_layout(p.Tpad, p.n, p.R);
+    for (int i = 0; i < p.n; ++i) {
+      const Question& q = qs[p.b0 + i];
+      memcpy(q.logits, h_out + h_meta[L.moff + i], (size_t)q.nmark * 4);
+      memcpy(q.act, h_out + Rcap + (size_t)i * cfg.n_act, (size_t)cfg.n_act * 4);
+    }
+  }
+
+  // Runs every question of `qs` (this replica's shard) through as many passes as needed.
+  int run(const std::vector<Question>& qs) {
+    if (qs.empty()) return 0;
+    if (cudaSetDevice(dev) != cudaSuccess) return -2;
+    std::vector<int> lens(qs.size()), nms(qs.size());
+    for (size_t i = 0; i < qs.size(); ++i) { lens[i] = qs[i].len; nms[i] = qs[i].nmark; }
+    std::vector<PassPlan> plans;
+    if (!plan_passes((int)qs.size(), lens.data(), nms.data(), E.pass_tokens, Bcap, Rcap, &plans)) return -1;
+    for (const PassPlan& p : plans) {
+      fill(p, qs.data());
+      const int rc = execute(p);
+      if (rc) return rc;
+      scatter(p, qs.data());
+    }
+    return 0;
+  }
+
+  // ------------------------------------------------------------------ benchmark staging
+  int stage_batch(const std::vector<Question>& qs) {
+    if (cudaSetDevice(dev) != cudaSuccess) return -2;
+    staged = qs;
+    if (staged_graph) { cudaGraphExecDestroy(staged_graph); staged_graph = nullptr; }
+    if (qs.empty()) return 0;
+    std::vector<int> lens(qs.size()), nms(qs.size());
+    for (size_t i = 0; i < qs.size(); ++i) { lens[i] = qs[i].len; nms[i] = qs[i].nmark; }
+    std::vector<PassPlan> plans;
+    if (!plan_passes((int)qs.size(), lens.data(), nms.data(), E.pass_tokens, Bcap, Rcap, &plans)) return -1;
+    if (plans.size() != 1) return -3;  // the staged batch must be one pass
+    staged_plan = plans[0];
+    fill(staged_plan, staged.data());
+    first_err = cudaSuccess;
+    chk(cudaMemcpyAsync(d_meta, h_meta, meta_layout(staged_plan.Tpad, staged_plan.n, staged_plan.R).total * 4,
+                        cudaMemcpyHostToDevice, st));
+    chk(cudaStreamSynchronize(st));
+    cudaGraph_t g = nullptr;
+    if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return -2;
+    capturing = true;
+    pass_launches = 0;
+    enqueue(staged_plan, false, false);  // inputs stay resident in HBM; outputs stay on the device
+    staged_launches = pass_launches;
+    capturing = false;
+    if (cudaStreamEndCapture(st, &g) != cudaSuccess || first_err != cudaSuccess) return -2;
+    const cudaError_t ie = cudaGraphInstantiate(&staged_graph, g, 0);
+    cudaGraphDestroy(g);
+    return ie == cudaSuccess ? 0 : -2;
+  }
+  int replay(int iters, double* ms) {
+    *ms = 0.0;
+    if (staged.empty()) return 0;
+    if (!staged_graph) return -4;
+    if (cudaSetDevice(dev) != cudaSuccess) return -2;
+    // a forward call since staging may have reused the metadata buffers: upload the staged pass again
+    fill(staged_plan, staged.data());
+    if (cudaMemcpy(d_meta, h_meta, meta_layout(staged_plan.Tpad, staged_plan.n, staged_plan.R).total * 4,
+                   cudaMemcpyHostToDevice) != cudaSuccess)
+      return -2;
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    first_err = cudaSuccess;
+    chk(cudaEventRecord(a, st));
+    for (int i = 0; i < iters; ++i) chk(cudaGraphLaunch(staged_graph, st));
+    n_launches += (long long)iters * staged_launches;
+    chk(cudaEventRecord(b, st));
+    chk(cudaEventSynchronize(b));
+    float f = 0.f;
+    cudaEventElapsedTime(&f, a, b);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    *ms = f;
+    int herr = 0;
+    cudaMemcpy(&herr, d_err, 4, cudaMemcpyDeviceToHost);
+    return first_err == cudaSuccess && herr == 0 ? 0 : -2;
+  }
+  int staged_results() {
+    if (staged.empty()) return 0;
+    if (cudaSetDevice(dev) != cudaSuccess) return -2;
+    const PassPlan& p = staged_plan;
+    fill(p, staged.data());
+    if (cudaMemcpy(h_out, d_logits, (size_t)p.KT * 4, cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(h_out + Rcap, d_act, (size_t)p.n * cfg.n_act * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+      return -2;
+    scatter(p, staged.data());
+    return 0;
+  }
+};
+
+// ===================================================================== Engine
+Engine::Engine() = default;
+Engine::~Engine() { reps.clear(); }
+
+bool Engine::load(const std::string& dir, int prec, const std::string& devices, std::string* err) {
+  try {
+    cfg = Config::load(dir + "/encoder/config.json", dir + "/rl_agent_config.json");
+  } catch (const std::exception& e) {
+    *err = e.what();
+    return false;
+  }
+  precision = prec;
+  if (const char* p = getenv("LAYA_PRECISION")) {
+    if (prec == 0 && (!strcmp(p, "fp32parity") || !strcmp(p, "fp32") || !strcmp(p, "1"))) precision = 1;
+  }
+  if (cfg.head_dim != 64 || cfg.d % 128 != 0 || cfg.d > 1024 || cfg.intermediate % 64 != 0 || cfg.head_layers < 1 ||
+      cfg.n_act < 1 || cfg.n_act > 256 || cfg.max_len < 1) {
+    *err = "unsupported model shape (needs head_dim 64, d a multiple of 128 up to 1024, intermediate a multiple of "
+           "64, 1+ head layers, 1..256 act outputs)";
+    return false;
+  }
+  if (getenv("LAYA_VERBOSE")) cfg.dump();
+  max_tokens = std::max(env_int("LAYA_MAX_TOKENS", 131072), cfg.max_len);
+  pass_tokens = std::min(std::max(env_int("LAYA_PASS_TOKENS", max_tokens), cfg.max_len), max_tokens);
+  max_seqs = std::max(env_int("LAYA_MAX_SEQS", 4096), 1);
+  max_gathered = std::max(max_tokens / 4, 2 * (kMaxMarkers + 1));
+  use_graphs = env_int("LAYA_GRAPHS", 1) != 0;
+  prof_on = getenv("LAYA_PROFILE") != nullptr;
+  if (const char* d = getenv("LAYA_DUMP_DIR")) dump_dir = d;
+
+  std::vector<int> devs;
+  std::string list = devices;
+  if (list.empty() && getenv("LAYA_DEVICES")) list = getenv("LAYA_DEVICES");
+  for (size_t i = 0; i < list.size();) {
+    size_t j = list.find(',', i);
+    if (j == std::string::npos) j = list.size();
+    if (j > i) devs.push_back(atoi(list.substr(i, j - i).c_str()));
+    i = j + 1;
+  }
+  if (devs.empty()) {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess) { *err = "no CUDA device"; return false; }
+    devs.push_back(d);
+  }
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) { *err = "no CUDA device"; return false; }
+  for (int d : devs)
+    if (d < 0 || d >= ndev) { *err = "bad device ordinal in device list"; return false; }
+
+  SafeTensors W;
+  if (!W.open(dir + "/model.safetensors", err)) return false;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  std::vector<std::string> errs(devs.size());
+  std::vector<int> ok(devs.size(), 0);
+  for (int d : devs) reps.emplace_back(new Replica(*this, d));
+  std::vector<std::thread> th;
+  for (size_t i = 0; i < devs.size(); ++i)
+    th.emplace_back([&, i] { ok[i] = reps[i]->load(W, &errs[i]) ? 1 : 0; });
+  for (auto& t : th) t.join();
+  cudaSetDevice(prev);
+  for (size_t i = 0; i < devs.size(); ++i)
+    if (!ok[i]) { *err = "device " + std::to_string(devs[i]) + ": " + errs[i]; return false; }
+  if (getenv("LAYA_VERBOSE"))
+    printf("[laya] ready: %zu device(s) max_tokens/pass=%d graphs=%d precision=%s\n", reps.size(), pass_tokens,
+           (int)use_graphs, precision ? "fp32parity" : "bf16");
+  return true;
+}
+
+// Longest-processing-time-first assignment of questions to replicas on their length, keeping the
+// input order inside each shard.
+std::vector<std::vector<Question>> Engine::shard(int B, const int* lens, const int* ids, const int* nmark,
+                                                 const int* markers, const int* qtypes, float* logits, float* act) {
+  const int G = (int)reps.size();
+  std::vector<Question> all(B);
+  size_t io = 0, mo = 0;
+  for (int b = 0; b < B; ++b) {
+    all[b] = Question{lens[b], nmark[b], qtypes[b], ids + io, markers + mo, logits + mo, act + (size_t)b * cfg.n_act};
+    io += lens[b];
+    mo += nmark[b];
+  }
+  std::vector<std::vector<Question>> out(G);
+  if (G == 1) {
+    out[0] = std::move(all);
+    return out;
+  }
+  std::vector<int> order(B);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return lens[a] > lens[b]; });
+  std::vector<long long> load(G, 0);
+  std::vector<int> owner(B);
+  for (int b : order) {
+    const int g = (int)(std::min_element(load.begin(), load.end()) - load.begin());
+    owner[b] = g;
+    load[g] += lens[b] + 64;  // + per-question fixed cost
+  }
+  for (int b = 0; b < B; ++b) out[owner[b]].push_back(all[b]);
+  return out;
+}
+
+int Engine::forward_batch(int B, const int* lens, const int* ids, const int* nmark, const int* markers,
+                          const int* qtypes, float* logits, float* act) {
+  if (!validate_batch(B, lens, nmark, markers, cfg.max_len)) return -1;
+  if (B == 0) return 0;
+  auto shards = shard(B, lens, ids, nmark, markers, qtypes, logits, act);
+  if (reps.size() == 1) return reps[0]->run(shards[0]);
+  std::vector<int> rc(reps.size(), 0);
+  std::vector<std::thread> th;
+  for (size_t i = 1; i < reps.size(); ++i) th.emplace_back([&, i] { rc[i] = reps[i]->run(shards[i]); });
+  rc[0] = reps[0]->run(shards[0]);
+  for (auto& t : th) t.join();
+  for (int r : rc)
+    if (r) return r;
+  return 0;
+}
+
+int Engine::stage(int B, const int* lens, const int* ids, const int* nmark, const int* markers, const int* qtypes) {
+  if (!validate_batch(B, lens, nmark, markers, cfg.max_len)) return -1;
+  // keep private copies: the staged pass replays them
+  size_t nt = 0, nk = 0;
+  for (int b = 0; b < B; ++b) { nt += lens[b]; nk += nmark[b]; }
+  st_lens_.assign(lens, lens + B);
+  st_ids_.assign(ids, ids + nt);
+  st_nmark_.assign(nmark, nmark + B);
+  st_markers_.assign(markers, markers + nk);
+  st_qt_.assign(qtypes, qtypes + B);
+  st_B_ = B;
+  static thread_local std::vector<float> sink;
+  sink.assign(nk + (size_t)B * cfg.n_act + 1, 0.f);
+  auto shards = shard(B, st_lens_.data(), st_ids_.data(), st_nmark_.data(), st_markers_.data(), st_qt_.data(),
+                      sink.data(), sink.data() + nk);
+  std::vector<int> rc(reps.size(), 0);
+  std::vector<std::thread> th;
+  for (size_t i = 0; i < reps.size(); ++i) th.emplace_back([&, i] { rc[i] = reps[i]->stage_batch(shards[i]); });
+  for (auto& t : th) t.join();
+  for (int r : rc)
+    if (r) return r;
+  return 0;
+}
+
+int Engine::replay(int iters, double* ms) {
+  std::vector<int> rc(reps.size(), 0);
+  std::vector<double> t(reps.size(), 0.0);
+  std::vector<std::thread> th;
+  for (size_t i = 0; i < reps.size(); ++i) th.emplace_back([&, i] { rc[i] = reps[i]->replay(iters, &t[i]); });
+  for (auto& x : th) x.join();
+  *ms = *std::max_element(t.begin(), t.end());
+  for (int r : rc)
+    if (r) return r;
+  return 0;
+}
+
+int Engine::staged_results(float* logits, float* act) {
+  if (st_B_ == 0) return 0;
+  auto shards = shard(st_B_, st_lens_.data(), st_ids_.data(), st_nmark_.data(), st_markers_.data(), st_qt_.data(),
+                      logits, act);
+  for (size_t i = 0; i < reps.size(); ++i) {
+    reps[i]->staged = shards[i];
+    const int r = reps[i]->staged_results();
+    if (r) return r;
+  }
+  return 0;
+}
+
+void Engine::prof_report(int iters) {
+  std::vector<std::pair<std::string, std::pair<double, long long>>> acc;
+  for (auto& r : reps)
+    for (auto& kv : r->prof_acc) {
+      bool f = false;
+      for (auto& a : acc)
+        if (a.first == kv.first) { a.second.first += kv.second.first; a.second.second += kv.second.second; f = true; }
+      if (!f) acc.push_back(kv);
+    }
+  if (acc.empty()) return;
+  double tot = 0;
+  for (auto& kv : acc) tot += kv.second.first;
+  std::sort(acc.begin(), acc.end(), [](auto& a, auto& b) { return a.second.first > b.second.first; });
+  iters = iters > 0 ? iters : 1;
+  printf("\n%-18s %9s %7s %9s\n", "stage", "ms/fwd", "%", "launches");
+  for (auto& kv : acc)
+    printf("%-18s %9.3f %6.1f%% %9lld\n", kv.first.c_str(), kv.second.first / iters, 100 * kv.second.first / tot,
+           kv.second.second);
+  printf("%-18s %9.3f (device time, stages back to back)\n", "TOTAL", tot / iters);
+}
+
+void Engine::prof_reset() {
+  for (auto& r : reps) r->prof_acc.clear();
+}
+
+int Engine::prof_get(const std::string& name, double* ms, long long* launches) {
+  double m = 0;
+  long long n = 0;
+  bool found = false;
+  for (auto& r : reps)
+    for (auto& kv : r->prof_acc)
+      if (kv.first == name) { m += kv.second.first; n += kv.second.second; found = true; }
+  if (ms) *ms = m;
+  if (launches) *launches = n;
+  return found ? 0 : -1;
+}
+
+void Engine::io_stats(long long* launches, long long* h2d, long long* d2h, bool reset) {
+  long long a = 0, b = 0, c = 0;
+  for (auto& r : reps) {
+    a += r->n_launches;
+    b += r->n_h2d;
+    c += r->n_d2h;
+    if (reset) r->n_launches = r->n_h2d = r->n_d2h = 0;
+  }
+  if (launches) *launches = a;
+  if (h2d) *h2d = b;
+  if (d2h) *d2h = c;
+}
+
+void Engine::tune_all() {
+  // The GEMM tile width is chosen per launch from the tile count (pick_bn); nothing to pre-tune.
+}
+
+}  // namespace laya

@@ -9,6 +9,7 @@
 //               TMEM accumulators, so the epilogue of tile i overlaps the main loop of tile i+1
 //   warps 2..5  epilogue: tcgen05.ld of their 32-lane TMEM quarter (one output row per thread), the
 //               fused math (bias / ReLU / GELU / RoPE / GeGLU / fp32 residual add) and the stores.
+// gemm_prepare_device() must run once per device (it raises the dynamic shared-memory limit).
 // Tiles are walked in row-block-major order with N fastest, so the CTAs in flight share one weight
 // matrix through L2 and read each activation row block from HBM once.
 #include "common.cuh"
@@ -86,17 +87,20 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row, int nb, c
                                               const GemmEpi& ep) {
   const bool valid = row < sh.M;
   if constexpr (EPI == EPI_GEGLU) {
-    const int half = BN / 2;
-    const int gt = min(half, ep.geglu_I - nb * half);  // input (then gate) columns in this tile
-    for (int c = 0; c < gt; c += 32) {
-      float xin[32], gate[32];
-      __syncwarp();
-      tmem_ld32(tbase + c, xin);
-      tmem_ld32(tbase + gt + c, gate);
-      if (valid) {
+    // B rows are interleaved in groups of 64: [64 input rows, their 64 gate rows] per 128 columns.
+    for (int s = 0; s < BN; s += 128) {
+      const int ocol = nb * (BN / 2) + s / 2;  // first output column of this 128-column group
+      if (ocol >= ep.geglu_I) break;
+      for (int c = 0; c < 64; c += 32) {
+        float xin[32], gate[32];
+        __syncwarp();
+        tmem_ld32(tbase + s + c, xin);
+        tmem_ld32(tbase + s + 64 + c, gate);
+        if (valid) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) xin[i] = gelu_erf(xin[i]) * gate[i];
-        store_row32(xin, ep, (long long)row * ep.ld + nb * half + c);
+          for (int i = 0; i < 32; ++i) xin[i] = gelu_erf(xin[i]) * gate[i];
+          store_row32(xin, ep, (long long)row * ep.ld + ocol + c);
+        }
       }
     }
   } else if constexpr (EPI == EPI_ROPE) {
@@ -307,16 +311,15 @@ EncodeTiledFn encode_fn() {
 }
 
 template <int BN, int EPI>
+cudaError_t prepare_one() {
+  return cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)gemm_smem_bytes<BN>());
+}
+
+template <int BN, int EPI>
 cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmShape& sh, const GemmEpi& ep,
                        int* err, int grid_ctas, cudaStream_t st) {
-  static bool attr_set = false;  // per process; the attribute is per function, not per device
   constexpr size_t smem = gemm_smem_bytes<BN>();
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
   const int tiles = ((sh.M + kBM - 1) / kBM) * ((sh.N + BN - 1) / BN);
   const int grid = tiles < grid_ctas ? tiles : grid_ctas;
   if (grid <= 0) return cudaSuccess;
@@ -353,11 +356,20 @@ bool make_operand_map(CUtensorMap* map, const void* base, uint64_t K, uint64_t r
   return r == CUDA_SUCCESS;
 }
 
+cudaError_t gemm_prepare_device() {
+  cudaError_t e = cudaSuccess;
+  for (cudaError_t r : {prepare_one<128, EPI_STORE>(), prepare_one<128, EPI_ROPE>(), prepare_one<128, EPI_GEGLU>(),
+                        prepare_one<128, EPI_RESID>(), prepare_one<256, EPI_STORE>(), prepare_one<256, EPI_ROPE>(),
+                        prepare_one<256, EPI_GEGLU>(), prepare_one<256, EPI_RESID>()})
+    if (r != cudaSuccess) e = r;
+  return e;
+}
+
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, int bn, const GemmShape& sh,
                         const GemmEpi& ep, int* err, int grid_ctas, cudaStream_t st) {
   if (sh.M <= 0) return cudaSuccess;
   if (sh.N % 32 != 0 || sh.K % 8 != 0 || (sh.nseg != 1 && sh.nseg != 3)) return cudaErrorInvalidValue;
-  if (ep.kind == EPI_GEGLU && (ep.geglu_I % 32 != 0 || sh.N != 2 * ep.geglu_I)) return cudaErrorInvalidValue;
+  if (ep.kind == EPI_GEGLU && (ep.geglu_I % 64 != 0 || sh.N != 2 * ep.geglu_I)) return cudaErrorInvalidValue;
   if (ep.kind == EPI_ROPE && (ep.rope_cols % 64 != 0 || !ep.pos || !ep.cos_t || !ep.sin_t))
     return cudaErrorInvalidValue;
   if (ep.kind == EPI_RESID ? ep.resid == nullptr : ep.out == nullptr) return cudaErrorInvalidValue;

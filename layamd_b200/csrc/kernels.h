@@ -21,7 +21,7 @@ enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2 };
 
 struct GemmShape {
   int M;     // rows of A that are valid (rows beyond are computed from whatever the buffer holds and never stored)
-  int N;     // rows of B (for EPI_GEGLU: 2*I, interleaved in groups of BN/2)
+  int N;     // rows of B (for EPI_GEGLU: 2*I, interleaved as [64 input rows, their 64 gate rows]...)
   int K;     // reduction length of one segment
   int nseg;  // 1 (bf16) or 3 (split-bf16 fp32 emulation)
 };
@@ -39,13 +39,17 @@ struct GemmEpi {
   const float* sin_t = nullptr;
   const int* pos = nullptr;      // EPI_ROPE: position of each row within its sequence
   int rope_cols = 0;             // EPI_ROPE: rotate columns [0, rope_cols) (q and k), head dim 64
-  int geglu_I = 0;               // EPI_GEGLU: output width I
+  int geglu_I = 0;               // EPI_GEGLU: output width I (a multiple of 64)
 };
 
 // Builds a 3-D tensor map {K, rows, planes} over a bf16 operand with a {64, box_rows, 1} box and the
 // 128-byte swizzle. Returns false if the driver rejects it (alignment).
 bool make_operand_map(CUtensorMap* map, const void* base, uint64_t K, uint64_t rows, uint64_t planes,
                       uint32_t box_rows);
+
+// Raises the dynamic shared-memory limit of every GEMM instantiation on the current device; call
+// once per device before the first gemm_launch there.
+cudaError_t gemm_prepare_device();
 
 // bn is 128 or 256 and must match the box height of `tb`. `grid_ctas` caps the persistent grid.
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, int bn, const GemmShape& sh,
@@ -68,7 +72,8 @@ struct AttnArgs {
   int n_items;
   const int* soff;       // [B] first packed row of each sequence
   const int* slen;       // [B] sequence length
-  const int* gsrc;       // gathered mode: packed row of each gathered query
+  const int* gsrc;       // gathered mode: packed row of each listed query
+  const int* gdst;       // gathered mode: output row of each listed query
   int gathered;          // 0: contiguous query blocks, 1: gathered queries (full attention)
   int H;                 // heads (head dim is 64)
   int window;            // half window (|q-k| <= window), 0 = global
@@ -96,6 +101,7 @@ struct LnArgs {
   float* out_f32 = nullptr;       // write y as fp32 (may alias src when no gather)
   const float* w2 = nullptr;      // second LayerNorm (optional)
   const float* b2 = nullptr;
+  float eps2 = 1e-5f;
   bf16* out_bf = nullptr;         // write (second LN ? z : y) as bf16 planes
   int out_planes = 1;
   long long out_plane = 0;

@@ -1,0 +1,193 @@
+// Row kernels of the Laya B200 engine: the LayerNorm family and the decision-head outputs.
+//
+// ln_kernel replaces the reference's k_ln (embedding gather + LN, src/kernels.hip:35-64), the LN half
+// of k_res_ln (src/kernels.hip:105-137; the residual add itself is fused into the GEMM epilogue here)
+// and k_gather (src/kernels.hip:267-271). One warp owns one row of D = 128*NV fp32 values held in
+// registers as float4 (16-byte coalesced loads and stores); mean and variance are two-pass in fp32 and
+// the normaliser is 1/sqrt(var + eps), as torch.nn.LayerNorm computes it. Optional outputs: the fp32
+// source row (gather), the normalised fp32 row (may overwrite the source in place: the final norm +
+// type embedding is written back into the residual stream), and bf16 planes of either the normalised
+// row or a second LayerNorm of it (the next layer's input, hi/lo planes in fp32-parity mode).
+//
+// head_out_kernel replaces k_bias_to_float + k_act_head (src/kernels.hip:273-307): per question, the
+// scorer's final Linear(d, 1) at each option marker, softmax features of those logits and the act
+// head MLP on the question's CLS row.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace laya {
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int NV>
+__device__ __forceinline__ void layer_norm_regs(float4 (&v)[NV], const float* w, const float* b, float eps, int D,
+                                                int lane) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  const float mean = warp_sum(s) / D;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    v[i].x -= mean; v[i].y -= mean; v[i].z -= mean; v[i].w -= mean;
+    q += (v[i].x * v[i].x + v[i].y * v[i].y) + (v[i].z * v[i].z + v[i].w * v[i].w);
+  }
+  const float rstd = 1.f / sqrtf(warp_sum(q) / D + eps);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float4 g = reinterpret_cast<const float4*>(w)[lane + 32 * i];
+    float4 r = make_float4(v[i].x * rstd * g.x, v[i].y * rstd * g.y, v[i].z * rstd * g.z, v[i].w * rstd * g.w);
+    if (b) {
+      const float4 bb = reinterpret_cast<const float4*>(b)[lane + 32 * i];
+      r.x += bb.x; r.y += bb.y; r.z += bb.z; r.w += bb.w;
+    }
+    v[i] = r;
+  }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256) ln_kernel(const LnArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= a.rows) return;
+  const int D = a.D;
+  const long long src_row = a.ids ? (long long)a.ids[row] : a.gidx ? (long long)a.gidx[row] : (long long)row;
+  const float4* src = reinterpret_cast<const float4*>(a.src + src_row * D);
+  float4 v[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) v[i] = src[lane + 32 * i];
+  if (a.copy_f32) {
+    float4* c = reinterpret_cast<float4*>(a.copy_f32 + (long long)row * D);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) c[lane + 32 * i] = v[i];
+  }
+  if (a.w) {
+    layer_norm_regs<NV>(v, a.w, a.b, a.eps, D, lane);
+    if (a.type_emb) {
+      const int s = a.rowseq[row];
+      if (s >= 0) {
+        const float4* t = reinterpret_cast<const float4*>(a.type_emb + (long long)a.qtype[s] * D);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const float4 tt = t[lane + 32 * i];
+          v[i].x += tt.x; v[i].y += tt.y; v[i].z += tt.z; v[i].w += tt.w;
+        }
+      }
+    }
+  }
+  if (a.out_f32) {
+    float4* y = reinterpret_cast<float4*>(a.out_f32 + (long long)row * D);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) y[lane + 32 * i] = v[i];
+  }
+  if (a.out_bf) {
+    if (a.w2) layer_norm_regs<NV>(v, a.w2, a.b2, a.eps2, D, lane);
+    uint2* hi = reinterpret_cast<uint2*>(a.out_bf + (long long)row * D);
+    uint2* lo = reinterpret_cast<uint2*>(a.out_bf + a.out_plane + (long long)row * D);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint32_t h0 = pack_bf16x2(v[i].x, v[i].y), h1 = pack_bf16x2(v[i].z, v[i].w);
+      hi[lane + 32 * i] = make_uint2(h0, h1);
+      if (a.out_planes == 2) {
+        const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h0));
+        const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h1));
+        lo[lane + 32 * i] = make_uint2(pack_bf16x2(v[i].x - f0.x, v[i].y - f0.y), pack_bf16x2(v[i].z - f1.x, v[i].w - f1.y));
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) head_out_kernel(const HeadOutArgs a) {
+  __shared__ float s_logit[256];
+  __shared__ float s_in[1024 + 8];
+  __shared__ float s_hid[256];
+  const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int D = a.D, nm = a.nmark[b], mo = a.moff[b];
+  // scorer output Linear(d, 1) at every option marker of this question
+  for (int k = warp; k < nm; k += 8) {
+    const long long row = mo + k;
+    float s = 0.f;
+    if (a.hs_f32) {
+      const float* hr = static_cast<const float*>(a.hs) + row * D;
+      for (int i = lane; i < D; i += 32) s = fmaf(hr[i], a.w3[i], s);
+    } else {
+      const bf16* hr = static_cast<const bf16*>(a.hs) + row * D;
+      for (int i = lane; i < D; i += 32) s = fmaf(__bfloat162float(hr[i]), a.w3[i], s);
+    }
+    s = warp_sum(s) + a.b3;
+    if (lane == 0) {
+      s_logit[k] = s;
+      a.logits[mo + k] = s;
+    }
+  }
+  for (int i = tid; i < D; i += 256) s_in[i] = a.cls[(long long)b * D + i];
+  __syncthreads();
+  if (tid == 0) {
+    // softmax over the question's option logits -> [top1, top1-top2, entropy/log(max(k,2)), max(k,2)/255]
+    float mx = -INFINITY;
+    for (int i = 0; i < nm; ++i) mx = fmaxf(mx, s_logit[i]);
+    float sum = 0.f;
+    for (int i = 0; i < nm; ++i) sum += expf(s_logit[i] - mx);
+    float t1 = 0.f, t2 = 0.f, ent = 0.f;
+    for (int i = 0; i < nm; ++i) {
+      const float p = expf(s_logit[i] - mx) / sum;
+      ent -= p * logf(fmaxf(p, 1e-9f));
+      if (p > t1) { t2 = t1; t1 = p; } else if (p > t2) { t2 = p; }
+    }
+    const float k = (float)(nm < 2 ? 2 : nm);
+    s_in[D] = t1;
+    s_in[D + 1] = t1 - t2;
+    s_in[D + 2] = ent / logf(k);
+    s_in[D + 3] = k / 255.f;
+  }
+  __syncthreads();
+  const int K0 = D + 4;
+  for (int j = warp; j < 256; j += 8) {
+    const float* wr = a.w0 + (long long)j * K0;
+    float s = 0.f;
+    for (int i = lane; i < K0; i += 32) s = fmaf(wr[i], s_in[i], s);
+    s = warp_sum(s);
+    if (lane == 0) s_hid[j] = gelu_erf(s + a.b0[j]);
+  }
+  __syncthreads();
+  for (int j = warp; j < a.n_act; j += 8) {
+    const float* wr = a.w2 + (long long)j * 256;
+    float s = 0.f;
+    for (int i = lane; i < 256; i += 32) s = fmaf(wr[i], s_hid[i], s);
+    s = warp_sum(s);
+    if (lane == 0) a.act[(long long)b * a.n_act + j] = s + a.b2[j];
+  }
+}
+
+}  // namespace
+
+cudaError_t ln_launch(const LnArgs& a, cudaStream_t st) {
+  if (a.rows <= 0) return cudaSuccess;
+  if (a.D % 128 != 0 || a.D > 1024) return cudaErrorInvalidValue;
+  const int grid = (a.rows + 7) / 8;
+  switch (a.D / 128) {
+    case 1: ln_kernel<1><<<grid, 256, 0, st>>>(a); break;
+    case 2: ln_kernel<2><<<grid, 256, 0, st>>>(a); break;
+    case 3: ln_kernel<3><<<grid, 256, 0, st>>>(a); break;
+    case 4: ln_kernel<4><<<grid, 256, 0, st>>>(a); break;
+    case 5: ln_kernel<5><<<grid, 256, 0, st>>>(a); break;
+    case 6: ln_kernel<6><<<grid, 256, 0, st>>>(a); break;
+    case 7: ln_kernel<7><<<grid, 256, 0, st>>>(a); break;
+    case 8: ln_kernel<8><<<grid, 256, 0, st>>>(a); break;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t head_out_launch(const HeadOutArgs& a, cudaStream_t st) {
+  if (a.B <= 0) return cudaSuccess;
+  if (a.D > 1024 || a.n_act > 256) return cudaErrorInvalidValue;
+  head_out_kernel<<<a.B, 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace laya

@@ -151,8 +151,8 @@ def test_rope(L, bn):
     assert rel(out, ref) < 1e-4
 
 
-def interleave_geglu(W, I, group):
-    """[2I, K] (input rows then gate rows) -> groups of `group` input rows followed by their gate rows."""
+def interleave_geglu(W, I, group=64):
+    """[2I, K] (input rows then gate rows) -> groups of 64 input rows followed by their gate rows."""
     parts = []
     for j in range(0, I, group):
         g = min(group, I - j)
@@ -161,14 +161,14 @@ def interleave_geglu(W, I, group):
     return torch.cat(parts).contiguous()
 
 
-@pytest.mark.parametrize("I,bn", [(2624, 256), (1152, 256), (2624, 128)])
+@pytest.mark.parametrize("I,bn", [(2624, 256), (1152, 256), (2624, 128), (192, 256)])
 def test_geglu(L, I, bn):
     M, K = 513, 1024
     g = torch.Generator(device="cuda").manual_seed(I)
     A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
     W = (0.03 * torch.randn(2 * I, K, device="cuda", generator=g)).bfloat16()
     out = torch.empty((M, I), device="cuda")
-    gemm(L, A, interleave_geglu(W, I, bn // 2), out, M, 2 * I, K, epi=EPI_GEGLU, geglu_I=I, bn=bn)
+    gemm(L, A, interleave_geglu(W, I), out, M, 2 * I, K, epi=EPI_GEGLU, geglu_I=I, bn=bn)
     y = A.double() @ W.double().T
     ref = torch.nn.functional.gelu(y[:, :I]) * y[:, I:]
     assert rel(out, ref) < 1e-4
