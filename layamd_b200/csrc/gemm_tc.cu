@@ -38,6 +38,7 @@ struct GemmSmem {
   uint64_t drain;
   uint32_t tmem;
   int abort;
+  alignas(16) float stg[4][32 * 32];  // epilogue staging, one 32 x 32 fp32 tile per epilogue warp
 };
 
 template <int BN>
@@ -51,40 +52,81 @@ __device__ __forceinline__ float apply_act(float v, int act) {
   return v;
 }
 
-// Stores 32 consecutive values of one row. off is the element offset of the first value.
-__device__ __forceinline__ void store_row32(const float (&v)[32], const GemmEpi& ep, long long off) {
-  if (ep.out_mode == OUT_F32) {
-    float4* p = reinterpret_cast<float4*>(static_cast<float*>(ep.out) + off);
+// Per-warp staging tile of the epilogue: 32 rows x 32 fp32, 16-byte chunks XOR-swizzled by row, so
+// both the row-per-thread writes (after tcgen05.ld) and the row-segment reads are bank-conflict free.
+__device__ __forceinline__ float* stg_at(float* stg, int r, int f) { return stg + r * 32 + ((f ^ (r & 7)) << 2); }
+
+__device__ __forceinline__ void stage_row(float* stg, int lane, const float (&v)[32]) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) p[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-    return;
+  for (int f = 0; f < 8; ++f)
+    *reinterpret_cast<float4*>(stg_at(stg, lane, f)) = make_float4(v[4 * f], v[4 * f + 1], v[4 * f + 2], v[4 * f + 3]);
+}
+
+// Coalesced write-out of one staged 32 x 32 chunk (rows row0.., columns col..col+31): lane l handles
+// 16 bytes (float4 l%8) of rows l/8 + 4k, so every warp instruction covers four 128-byte row
+// segments. `post` adds the bias and applies the activation; `resid` adds into the fp32 residual.
+template <bool RESID>
+__device__ __forceinline__ void write_chunk(float* stg, int lane, int row0, int col, const GemmShape& sh,
+                                            const GemmEpi& ep, bool post) {
+  const int f = lane & 7, j = lane >> 3;
+  float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (post && ep.bias) b4 = *reinterpret_cast<const float4*>(ep.bias + col + 4 * f);
+  float4 v[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    v[k] = *reinterpret_cast<const float4*>(stg_at(stg, 4 * k + j, f));
+    if (post) {
+      v[k].x += b4.x; v[k].y += b4.y; v[k].z += b4.z; v[k].w += b4.w;
+      if (ep.act != ACT_NONE) {
+        v[k].x = apply_act(v[k].x, ep.act); v[k].y = apply_act(v[k].y, ep.act);
+        v[k].z = apply_act(v[k].z, ep.act); v[k].w = apply_act(v[k].w, ep.act);
+      }
+    }
   }
-  bf16* base = static_cast<bf16*>(ep.out);
-  uint4* hi = reinterpret_cast<uint4*>(base + off);
-  uint32_t h[16];
+  if constexpr (RESID) {
+    float4 x[8];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) h[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) hi[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
-  if (ep.out_mode == OUT_BF16X2) {
-    uint4* lo = reinterpret_cast<uint4*>(base + ep.plane + off);
-    uint32_t l[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      __nv_bfloat162 hv = *reinterpret_cast<__nv_bfloat162*>(&h[i]);
-      float2 hf = __bfloat1622float2(hv);
-      l[i] = pack_bf16x2(v[2 * i] - hf.x, v[2 * i + 1] - hf.y);
+    for (int k = 0; k < 8; ++k) {  // all loads first: eight independent 16-byte requests in flight
+      const int row = row0 + 4 * k + j;
+      if (row < sh.M) x[k] = *reinterpret_cast<const float4*>(ep.resid + (long long)row * ep.ld + col + 4 * f);
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) lo[i] = make_uint4(l[4 * i], l[4 * i + 1], l[4 * i + 2], l[4 * i + 3]);
+    for (int k = 0; k < 8; ++k) {
+      const int row = row0 + 4 * k + j;
+      if (row < sh.M) {
+        x[k].x += v[k].x; x[k].y += v[k].y; x[k].z += v[k].z; x[k].w += v[k].w;
+        *reinterpret_cast<float4*>(ep.resid + (long long)row * ep.ld + col + 4 * f) = x[k];
+      }
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int row = row0 + 4 * k + j;
+      if (row >= sh.M) continue;
+      const long long off = (long long)row * ep.ld + col + 4 * f;
+      if (ep.out_mode == OUT_F32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(ep.out) + off) = v[k];
+      } else {
+        bf16* base = static_cast<bf16*>(ep.out);
+        const uint32_t h0 = pack_bf16x2(v[k].x, v[k].y), h1 = pack_bf16x2(v[k].z, v[k].w);
+        *reinterpret_cast<uint2*>(base + off) = make_uint2(h0, h1);
+        if (ep.out_mode == OUT_BF16X2) {
+          const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h0));
+          const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h1));
+          *reinterpret_cast<uint2*>(base + ep.plane + off) =
+              make_uint2(pack_bf16x2(v[k].x - f0.x, v[k].y - f0.y), pack_bf16x2(v[k].z - f1.x, v[k].w - f1.y));
+        }
+      }
+    }
   }
 }
 
-// Epilogue of one tile for one thread (one output row). Every tcgen05.ld is executed by the whole
-// warp; only the stores depend on the row being valid.
+// Epilogue of one tile for one warp (32 rows starting at row0; thread `lane` holds row row0+lane
+// after each tcgen05.ld). Every tcgen05.ld is executed by the whole warp; rows >= M are never stored.
 template <int BN, int EPI>
-__device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row, int nb, const GemmShape& sh,
-                                              const GemmEpi& ep) {
+__device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row0, int lane, int nb, const GemmShape& sh,
+                                              const GemmEpi& ep, float* stg) {
+  const int row = row0 + lane;
   const bool valid = row < sh.M;
   if constexpr (EPI == EPI_GEGLU) {
     // B rows are interleaved in groups of 64: [64 input rows, their 64 gate rows] per 128 columns.
@@ -96,14 +138,29 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row, int nb, c
         __syncwarp();
         tmem_ld32(tbase + s + c, xin);
         tmem_ld32(tbase + s + 64 + c, gate);
-        if (valid) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) xin[i] = gelu_erf(xin[i]) * gate[i];
-          store_row32(xin, ep, (long long)row * ep.ld + ocol + c);
-        }
+        for (int i = 0; i < 32; ++i) xin[i] = gelu_erf(xin[i]) * gate[i];
+        stage_row(stg, lane, xin);
+        __syncwarp();
+        write_chunk<false>(stg, lane, row0, ocol + c, sh, ep, false);
       }
     }
   } else if constexpr (EPI == EPI_ROPE) {
+    // cos/sin of this row's position are the same for every head: load them once per tile, as
+    // 16 independent 16-byte loads, and reuse them for the BN/64 heads of the tile.
+    float cs[32], sn[32];
+    const bool any_rot = nb * BN < ep.rope_cols;
+    if (any_rot && valid) {
+      const int p = ep.pos[row];
+      const float4* ct = reinterpret_cast<const float4*>(ep.cos_t + (size_t)p * 32);
+      const float4* st = reinterpret_cast<const float4*>(ep.sin_t + (size_t)p * 32);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 c4 = ct[i], s4 = st[i];
+        cs[4 * i] = c4.x; cs[4 * i + 1] = c4.y; cs[4 * i + 2] = c4.z; cs[4 * i + 3] = c4.w;
+        sn[4 * i] = s4.x; sn[4 * i + 1] = s4.y; sn[4 * i + 2] = s4.z; sn[4 * i + 3] = s4.w;
+      }
+    }
     for (int h = 0; h < BN; h += 64) {
       const int col = nb * BN + h;
       if (col >= sh.N) break;
@@ -111,27 +168,25 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row, int nb, c
       __syncwarp();
       tmem_ld32(tbase + h, x1);
       tmem_ld32(tbase + h + 32, x2);
-      if (valid) {
-        if (ep.bias) {
+      if (ep.bias) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) { x1[i] += ep.bias[col + i]; x2[i] += ep.bias[col + 32 + i]; }
-        }
-        if (col < ep.rope_cols) {
-          const int p = ep.pos[row];
-          const float* ct = ep.cos_t + (size_t)p * 32;
-          const float* st = ep.sin_t + (size_t)p * 32;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float c = ct[i], s = st[i];
-            const float a = x1[i], b = x2[i];
-            x1[i] = a * c - b * s;
-            x2[i] = b * c + a * s;
-          }
-        }
-        const long long off = (long long)row * ep.ld + col;
-        store_row32(x1, ep, off);
-        store_row32(x2, ep, off + 32);
+        for (int i = 0; i < 32; ++i) { x1[i] += ep.bias[col + i]; x2[i] += ep.bias[col + 32 + i]; }
       }
+      if (valid && col < ep.rope_cols) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float a = x1[i], b = x2[i];
+          x1[i] = a * cs[i] - b * sn[i];
+          x2[i] = b * cs[i] + a * sn[i];
+        }
+      }
+      stage_row(stg, lane, x1);
+      __syncwarp();
+      write_chunk<false>(stg, lane, row0, col, sh, ep, false);
+      __syncwarp();
+      stage_row(stg, lane, x2);
+      __syncwarp();
+      write_chunk<false>(stg, lane, row0, col + 32, sh, ep, false);
     }
   } else {
     for (int c = 0; c < BN; c += 32) {
@@ -140,26 +195,9 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row, int nb, c
       float v[32];
       __syncwarp();
       tmem_ld32(tbase + c, v);
-      if (!valid) continue;
-      if (ep.bias) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] += ep.bias[col + i];
-      }
-      if constexpr (EPI == EPI_RESID) {
-        float4* x = reinterpret_cast<float4*>(ep.resid + (long long)row * ep.ld + col);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float4 r = x[i];
-          r.x += v[4 * i]; r.y += v[4 * i + 1]; r.z += v[4 * i + 2]; r.w += v[4 * i + 3];
-          x[i] = r;
-        }
-      } else {
-        if (ep.act != ACT_NONE) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = apply_act(v[i], ep.act);
-        }
-        store_row32(v, ep, (long long)row * ep.ld + col);
-      }
+      stage_row(stg, lane, v);
+      __syncwarp();
+      write_chunk<EPI == EPI_RESID>(stg, lane, row0, col, sh, ep, true);
     }
   }
 }
@@ -273,12 +311,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t accph = (local >> 1) & 1;
-      if (!mbar_wait(smem_u32(&S.accf[acc]), accph, abort, err, kErrGemmAccFull)) break;
-      tc_fence_after();
       const int mb = t / num_n, nb = t - (t / num_n) * num_n;
       const int row = mb * kBM + q * 32 + lane;
+      if constexpr (EPI == EPI_RESID) {
+        // pull this tile's residual rows into L2 while its main loop is still running
+        if (row < sh.M) {
+          const int cols = min(BN, sh.N - nb * BN);
+          prefetch_l2_bulk(ep.resid + (long long)row * ep.ld + nb * BN, static_cast<uint32_t>(cols) * 4u);
+        }
+      }
+      if (!mbar_wait(smem_u32(&S.accf[acc]), accph, abort, err, kErrGemmAccFull)) break;
+      tc_fence_after();
       const uint32_t tbase = tmem + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue_tile<BN, EPI>(tbase, row, nb, sh, ep);
+      epilogue_tile<BN, EPI>(tbase, mb * kBM + q * 32, lane, nb, sh, ep, S.stg[q]);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&S.acce[acc]));
