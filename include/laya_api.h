@@ -110,7 +110,8 @@ int laya_set_dump_dir(void* h, const char* dir);
  * out = epilogue(A[planes][M][K] * W[planes][N][K]^T). epi: 0 store, 1 store with RoPE on columns
  * < rope_cols, 2 GeGLU (W interleaved in groups of bn/2, out has geglu_I columns), 3 fp32 residual
  * add into resid[M][N]. out_mode: 0 bf16, 1 bf16 hi/lo planes, 2 fp32. act: 0 none, 1 ReLU, 2 GELU.
- * bn: 128 or 256. planes 2 selects the three-product fp32 emulation. stream may be NULL. With
+ * bn: 128 or 256 (one CTA per 128 x bn tile) or 512 (a CTA pair per 256 x 256 tile, 2-SM MMA).
+ * planes 2 selects the three-product fp32 emulation. stream may be NULL. With
  * sync != 0 the call waits for the GPU and returns -100-code if the kernel reported an error. */
 int laya_b200_gemm(const void* A, const void* W, void* out, float* resid, const float* bias, int M, int N, int K,
                    int planes, int epi, int out_mode, int act, int bn, const float* cos_t, const float* sin_t,

@@ -37,7 +37,9 @@ extern "C" int laya_b200_gemm(const void* A, const void* W, void* out, float* re
   if ((planes != 1 && planes != 2) || M <= 0 || N <= 0 || K <= 0) return -2;
   CUtensorMap ta, tb;
   if (!make_operand_map(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)planes, 128)) return -3;
-  if (!make_operand_map(&tb, W, (uint64_t)K, (uint64_t)N, (uint64_t)planes, (uint32_t)bn)) return -3;
+  if (bn != 128 && bn != 256 && bn != kGemmPair) return -2;
+  const uint32_t box_b = bn == kGemmPair ? 128u : static_cast<uint32_t>(bn);  // a pair tile loads 128 B rows per CTA
+  if (!make_operand_map(&tb, W, (uint64_t)K, (uint64_t)N, (uint64_t)planes, box_b)) return -3;
   GemmShape sh{M, N, K, planes == 2 ? 3 : 1};
   GemmEpi ep;
   ep.kind = epi;

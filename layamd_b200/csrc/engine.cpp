@@ -116,7 +116,7 @@ class Replica {
  public:
   Engine& E;
   const Config& cfg;
-  int dev = 0, P = 1, nseg = 1, num_sms = 148;
+  int dev = 0, P = 1, nseg = 1, num_sms = 148, pair_clusters = 0;
   cudaStream_t st = nullptr;
   std::vector<void*> allocs;
   std::vector<void*> host_allocs;
@@ -258,6 +258,7 @@ class Replica {
     LAYA_TRY(cudaSetDevice(dev));
     LAYA_TRY(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev));
     LAYA_TRY(gemm_prepare_device());
+    pair_clusters = getenv("LAYA_NO_PAIR_GEMM") ? 0 : gemm_pair_clusters();
     LAYA_TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
     P = E.precision == 1 ? 2 : 1;
     nseg = P == 2 ? 3 : 1;
@@ -469,13 +470,17 @@ class Replica {
     ev_used = 0;
   }
 
-  int pick_bn(int M, const Mat& W) const {
+  // Tile per launch: the CTA-pair 256 x 256 tile when its tile count fills every co-resident pair
+  // twice, else 128 x 256, else 128 x 128 (more tiles for small M).
+  int pick_tile(int M, const Mat& W) const {
     if (W.N < 256) return 128;
+    const long long tp = (long long)((M + 255) / 256) * ((W.N + 255) / 256);
+    if (pair_clusters > 0 && tp >= 2LL * pair_clusters) return kGemmPair;
     const long long t256 = (long long)((M + 127) / 128) * ((W.N + 255) / 256);
     return t256 >= 2LL * num_sms ? 256 : 128;
   }
   void gemm(const Operand& A, int M, const Mat& W, const GemmEpi& ep) {
-    const int bn = pick_bn(M, W);
+    const int bn = pick_tile(M, W);
     GemmShape sh{M, W.N, W.K, nseg};
     launched(gemm_launch(A.map, bn == 256 ? W.m256 : W.m128, bn, sh, ep, d_err, num_sms, st));
   }

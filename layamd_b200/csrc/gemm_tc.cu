@@ -14,6 +14,7 @@
 // matrix through L2 and read each activation row block from HBM once.
 #include "common.cuh"
 #include "kernels.h"
+#include <algorithm>
 #include <cstdio>
 
 namespace laya {
@@ -339,6 +340,164 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ CTA-pair variant
+// The same pipeline on a cluster of two CTAs (one per SM) computing a 256 x 256 tile with the 2-SM
+// MMA (tcgen05.mma.cta_group::2): each CTA stages its own 128 rows of A and its own 128 rows of B, so
+// per output element each SM reads a third less operand data than the 128 x 256 single-CTA tile.
+// The even CTA issues the MMAs; both CTAs' TMA loads complete on the even CTA's `full` barrier, MMA
+// completion is committed to both CTAs' `empty` / `accf` barriers, and both CTAs' epilogue warps
+// arrive on the even CTA's `acce` barrier. Each CTA's epilogue owns its 128 accumulator rows.
+constexpr int kPairStages = 6;
+
+struct GemmSmemPair {
+  alignas(1024) bf16 a[kPairStages][128 * kBK];
+  alignas(1024) bf16 b[kPairStages][128 * kBK];
+  alignas(8) uint64_t full[kPairStages];
+  uint64_t empty[kPairStages];
+  uint64_t accf[2];
+  uint64_t acce[2];
+  uint64_t drain;
+  uint32_t tmem;
+  int abort;
+  alignas(16) float stg[4][32 * 32];
+};
+constexpr size_t gemm_pair_smem_bytes() { return sizeof(GemmSmemPair) + 1024; }
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                        const GemmShape sh, const GemmEpi ep, int* err) {
+  constexpr int BN = 256;
+  constexpr uint32_t kIdesc = idesc_bf16(256, BN);
+  constexpr uint32_t kPairStageBytes = 2u * (128 + 128) * kBK * 2;  // both CTAs' A and B halves
+  extern __shared__ uint8_t smem_raw[];
+  GemmSmemPair& S =
+      *reinterpret_cast<GemmSmemPair*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cid = static_cast<int>(cluster_id_x()), ncl = static_cast<int>(num_clusters_x());
+  const int num_n = (sh.N + BN - 1) / BN;
+  const int tiles = ((sh.M + 255) / 256) * num_n;
+  const int kb_seg = (sh.K + kBK - 1) / kBK;
+  const int nkb = kb_seg * sh.nseg;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) { mbar_init(smem_u32(&S.full[s]), 1); mbar_init(smem_u32(&S.empty[s]), 1); }
+    for (int a = 0; a < 2; ++a) { mbar_init(smem_u32(&S.accf[a]), 1); mbar_init(smem_u32(&S.acce[a]), 8); }
+    mbar_init(smem_u32(&S.drain), 1);
+    S.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&ta); tma_prefetch_desc(&tb); }
+  if (warp == 1) { tmem_alloc_pair(smem_u32(&S.tmem), 2 * BN); tmem_relinquish_pair(); }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers are initialised before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem = S.tmem;
+  volatile int* abort = &S.abort;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      uint32_t issued_mask = 0, last_phase = 0;
+      for (int t = cid; t < tiles; t += ncl) {
+        const int mb = t / num_n, nb = t - (t / num_n) * num_n;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(smem_u32(&S.empty[stage]), phase ^ 1, abort, err, kErrGemmEmpty)) { ok = false; break; }
+          const int seg = kb / kb_seg;
+          const int kk = (kb - seg * kb_seg) * kBK;
+          const int ap = seg == 2 ? 1 : 0, bp = seg == 1 ? 1 : 0;
+          const uint32_t fb = smem_u32(&S.full[stage]);
+          if (leader) mbar_expect_tx(fb, kPairStageBytes);
+          tma_load_3d_pair(smem_u32(S.a[stage]), &ta, kk, mb * 256 + (int)rank * 128, ap, fb);
+          tma_load_3d_pair(smem_u32(S.b[stage]), &tb, kk, nb * BN + (int)rank * 128, bp, fb);
+          issued_mask |= 1u << stage;
+          last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+      }
+      if (*abort && leader) {
+        const long long t0 = clock64();
+        for (int s = 0; s < kPairStages; ++s) {
+          if (!(issued_mask & (1u << s))) continue;
+          while (!mbar_try(smem_u32(&S.full[s]), (last_phase >> s) & 1)) {
+            if (clock64() - t0 > kWaitBudgetCycles) { atomicCAS(err, 0, kErrGemmDrain); break; }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      uint32_t stage = 0, phase = 0;
+      int local = 0;
+      for (int t = cid; t < tiles; t += ncl, ++local) {
+        const int acc = local & 1;
+        const uint32_t accph = (local >> 1) & 1;
+        if (!mbar_wait(smem_u32(&S.acce[acc]), accph ^ 1, abort, err, kErrGemmAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(smem_u32(&S.full[stage]), phase, abort, err, kErrGemmFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(S.a[stage]), b0 = smem_u32(S.b[stage]);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_bf16_pair(d, sdesc_k128(a0 + k * 32), sdesc_k128(b0 + k * 32), kIdesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit_pair(smem_u32(&S.empty[stage]), mapa_shared(smem_u32(&S.empty[stage]), 1));
+          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit_pair(smem_u32(&S.accf[acc]), mapa_shared(smem_u32(&S.accf[acc]), 1));
+      }
+      // every earlier commit has landed in both CTAs once this one has
+      umma_commit_pair(smem_u32(&S.drain), mapa_shared(smem_u32(&S.drain), 1));
+    }
+    if (lane == 0) {
+      const long long t0 = clock64();
+      while (!mbar_try(smem_u32(&S.drain), 0)) {
+        if (clock64() - t0 > kWaitBudgetCycles) { atomicCAS(err, 0, kErrGemmDrain); break; }
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const uint32_t acce_leader0 = mapa_shared(smem_u32(&S.acce[0]), 0);
+    const uint32_t acce_leader1 = mapa_shared(smem_u32(&S.acce[1]), 0);
+    int local = 0;
+    for (int t = cid; t < tiles; t += ncl, ++local) {
+      const int acc = local & 1;
+      const uint32_t accph = (local >> 1) & 1;
+      const int mb = t / num_n, nb = t - (t / num_n) * num_n;
+      const int row0 = mb * 256 + (int)rank * 128 + q * 32;
+      if constexpr (EPI == EPI_RESID) {
+        if (row0 + lane < sh.M) {
+          const int cols = min(BN, sh.N - nb * BN);
+          prefetch_l2_bulk(ep.resid + (long long)(row0 + lane) * ep.ld + nb * BN, static_cast<uint32_t>(cols) * 4u);
+        }
+      }
+      if (!mbar_wait(smem_u32(&S.accf[acc]), accph, abort, err, kErrGemmAccFull)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
+      epilogue_tile<BN, EPI>(tbase, row0, lane, nb, sh, ep, S.stg[q]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc ? acce_leader1 : acce_leader0);
+    }
+  }
+
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal or read its shared memory
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 2 * BN);
+  }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -384,7 +543,42 @@ cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmSh
   return cudaErrorInvalidValue;
 }
 
+constexpr int kMaxDevices = 64;
+int g_pair_clusters[kMaxDevices];  // co-resident CTA pairs per device (0: not measured yet)
+
+template <int EPI>
+cudaError_t prepare_pair(int* clusters) {
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)gemm_pair_smem_bytes());
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = gemm_pair_smem_bytes();
+  int n = 0;
+  e = cudaOccupancyMaxActiveClusters(&n, gemm_tc_pair_kernel<EPI>, &cfg);
+  if (e != cudaSuccess) return e;
+  if (*clusters == 0 || n < *clusters) *clusters = n;
+  return cudaSuccess;
+}
+
+template <int EPI>
+cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmShape& sh, const GemmEpi& ep, int* err,
+                        int clusters, cudaStream_t st) {
+  const int tiles = ((sh.M + 255) / 256) * ((sh.N + 255) / 256);
+  const int ncl = tiles < clusters ? tiles : clusters;
+  if (ncl <= 0) return cudaSuccess;
+  gemm_tc_pair_kernel<EPI><<<2 * ncl, kThreads, gemm_pair_smem_bytes(), st>>>(ta, tb, sh, ep, err);
+  return cudaGetLastError();
+}
+
 }  // namespace
+
+int gemm_pair_clusters() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+  return g_pair_clusters[dev];
+}
 
 bool make_operand_map(CUtensorMap* map, const void* base, uint64_t K, uint64_t rows, uint64_t planes,
                       uint32_t box_rows) {
@@ -407,6 +601,14 @@ cudaError_t gemm_prepare_device() {
                         prepare_one<128, EPI_RESID>(), prepare_one<256, EPI_STORE>(), prepare_one<256, EPI_ROPE>(),
                         prepare_one<256, EPI_GEGLU>(), prepare_one<256, EPI_RESID>()})
     if (r != cudaSuccess) e = r;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices) {
+    int clusters = 0;
+    for (cudaError_t r : {prepare_pair<EPI_STORE>(&clusters), prepare_pair<EPI_ROPE>(&clusters),
+                          prepare_pair<EPI_GEGLU>(&clusters), prepare_pair<EPI_RESID>(&clusters)})
+      if (r != cudaSuccess) e = r;
+    g_pair_clusters[dev] = clusters;
+  }
   return e;
 }
 
@@ -420,6 +622,16 @@ cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, int bn, co
   if (ep.kind == EPI_RESID ? ep.resid == nullptr : ep.out == nullptr) return cudaErrorInvalidValue;
   if (bn == 256) return launch_bn<256>(ta, tb, sh, ep, err, grid_ctas, st);
   if (bn == 128) return launch_bn<128>(ta, tb, sh, ep, err, grid_ctas, st);
+  if (bn == kGemmPair) {
+    const int clusters = std::min(gemm_pair_clusters(), grid_ctas / 2);
+    if (clusters <= 0) return cudaErrorInvalidConfiguration;
+    switch (ep.kind) {
+      case EPI_STORE: return launch_pair<EPI_STORE>(ta, tb, sh, ep, err, clusters, st);
+      case EPI_ROPE: return launch_pair<EPI_ROPE>(ta, tb, sh, ep, err, clusters, st);
+      case EPI_GEGLU: return launch_pair<EPI_GEGLU>(ta, tb, sh, ep, err, clusters, st);
+      case EPI_RESID: return launch_pair<EPI_RESID>(ta, tb, sh, ep, err, clusters, st);
+    }
+  }
   return cudaErrorInvalidValue;
 }
 

@@ -51,7 +51,13 @@ bool make_operand_map(CUtensorMap* map, const void* base, uint64_t K, uint64_t r
 // once per device before the first gemm_launch there.
 cudaError_t gemm_prepare_device();
 
-// bn is 128 or 256 and must match the box height of `tb`. `grid_ctas` caps the persistent grid.
+// Tile selector for gemm_launch: one CTA per 128 x 128 or 128 x 256 tile (bn = 128 / 256, `tb` box
+// height = bn), or a CTA pair per 256 x 256 tile with the 2-SM MMA (bn = kGemmPair, `tb` box 128).
+constexpr int kGemmPair = 512;
+// Co-resident CTA pairs of the pair kernel on the current device (set by gemm_prepare_device).
+int gemm_pair_clusters();
+
+// `grid_ctas` caps the persistent grid (CTAs; a pair counts as two).
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, int bn, const GemmShape& sh,
                         const GemmEpi& ep, int* err, int grid_ctas, cudaStream_t st);
 

@@ -1,0 +1,159 @@
+"""Isolated encoder-GEMM sweep (benchmark configuration C5) on the engine's tcgen05 GEMM.
+
+For M (packed tokens) in {512, 4096, 32768, 131072} and (K, N) in {(1024,3072), (1024,1024),
+(1024,5248), (2624,1024)} -- the Wqkv, Wo, Wi and MLP-out projections of ModernBERT-large -- times the
+kernel through the C ABI entry point ``laya_b200_gemm`` with CUDA events (warm-up, then `iters` back to
+back launches on one stream), in bf16 (one bf16 product, fp32 accumulation) and in fp32-parity mode
+(three bf16 products on hi/lo splits). Inputs: A ~ N(0,1), W ~ N(0,0.02), seed 5. Reports TFLOP/s
+(2MNK/t, parity mode counted as the same 2MNK), the fraction of the measured sustained and burst bf16
+peaks, the tile the engine would pick, torch.matmul (cuBLAS) on the same bf16 operands as a
+comparator, and max|C - C_ref| / max|C_ref| against an fp64 reference GEMM of the fp32 inputs.
+
+Usage: python -m layamd_b200.gemm_sweep [--m 512,4096] [--kn 1024x3072,...] [--epi store|geglu|rope|resid]
+       [--modes bf16,parity] [--tile auto|128|256|pair] [--iters 20] [--no-check] [--json]
+"""
+import argparse
+import ctypes
+import json
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+EPI = {"store": 0, "rope": 1, "geglu": 2, "resid": 3}
+TILES = {"128": 128, "256": 256, "pair": 512}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops_sustained"]), float(p["bf16_tflops"])
+    except Exception:
+        return 1400.0, 1590.0
+
+
+def pick_tile(M, N, sms):
+    """The engine's rule (engine.cpp pick_bn) for the single-CTA tiles."""
+    if N < 256:
+        return 128
+    return 256 if ((M + 127) // 128) * ((N + 255) // 256) >= 2 * sms else 128
+
+
+def interleave_geglu(W, I):
+    import torch
+    parts = []
+    for j in range(0, I, 64):
+        parts.append(W[j:j + 64])
+        parts.append(W[I + j:I + j + 64])
+    return torch.cat(parts).contiguous()
+
+
+def main():
+    import torch
+    from layamd_b200 import load_lib
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--m", default="512,4096,32768,131072")
+    ap.add_argument("--kn", default="1024x3072,1024x1024,1024x5248,2624x1024")
+    ap.add_argument("--epi", default="store", choices=sorted(EPI))
+    ap.add_argument("--modes", default="bf16,parity")
+    ap.add_argument("--tile", default="auto", choices=["auto"] + sorted(TILES))
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--no-check", action="store_true")
+    ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--json", action="store_true")
+    a = ap.parse_args()
+    L = load_lib()
+    dev = torch.device("cuda:0")
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    sus, burst = peaks()
+    st = torch.cuda.current_stream().cuda_stream
+    rows = []
+    for kn in a.kn.split(","):
+        K, N = (int(x) for x in kn.split("x"))
+        for M in (int(x) for x in a.m.split(",")):
+            g = torch.Generator(device=dev).manual_seed(5)
+            A32 = torch.randn(M, K, device=dev, generator=g)
+            W32 = 0.02 * torch.randn(N, K, device=dev, generator=g)
+            epi = EPI[a.epi]
+            I = N // 2
+            if epi == EPI["geglu"]:
+                W32 = interleave_geglu(W32, I)
+            ncols = I if epi == EPI["geglu"] else N
+            bn = pick_tile(M, N, sms) if a.tile == "auto" else TILES[a.tile]
+            pos = torch.randint(0, 512, (M,), device=dev, dtype=torch.int32, generator=g)
+            cos = torch.rand(512, 32, device=dev)
+            sin = torch.rand(512, 32, device=dev)
+            for mode in a.modes.split(","):
+                planes = 2 if mode == "parity" else 1
+                if planes == 1:
+                    A = A32.bfloat16().contiguous()
+                    W = W32.bfloat16().contiguous()
+                else:
+                    Ah = A32.bfloat16()
+                    Wh = W32.bfloat16()
+                    A = torch.stack([Ah, (A32 - Ah.float()).bfloat16()]).contiguous()
+                    W = torch.stack([Wh, (W32 - Wh.float()).bfloat16()]).contiguous()
+                out_mode = 2 if (planes == 2 or not a.no_check) else 0
+                out = torch.empty((M, ncols), device=dev, dtype=torch.float32 if out_mode == 2 else torch.bfloat16)
+                resid = torch.zeros((M, N), device=dev) if epi == EPI["resid"] else None
+
+                def run(sync=0):
+                    return L.laya_b200_gemm(ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(W.data_ptr()),
+                                            ctypes.c_void_p(out.data_ptr()),
+                                            ctypes.c_void_p(resid.data_ptr()) if resid is not None else None, None,
+                                            M, N, K, planes, epi, out_mode, 0, bn, ctypes.c_void_p(cos.data_ptr()),
+                                            ctypes.c_void_p(sin.data_ptr()), ctypes.c_void_p(pos.data_ptr()),
+                                            2 * (N // 3) // 64 * 64 if epi == EPI["rope"] else 0, I,
+                                            ctypes.c_void_p(st), sync)
+                rc = run(1)
+                assert rc == 0, rc
+                err = None
+                if not a.no_check and epi in (EPI["store"], EPI["resid"]):
+                    ref = A32.double() @ W32.double().T
+                    got = (resid if epi == EPI["resid"] else out).double()
+                    err = float((got - ref).abs().max() / ref.abs().max())
+                    del ref, got
+                for _ in range(a.warmup):
+                    run()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                e0.record()
+                for _ in range(a.iters):
+                    run()
+                e1.record()
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1) / a.iters
+                tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+                row = {"M": M, "K": K, "N": N, "mode": mode, "epi": a.epi, "tile": bn, "ms": ms, "tflops": tf,
+                       "frac_sustained": tf / sus, "frac_burst": tf / burst, "max_rel_err": err}
+                if mode == "bf16" and not a.no_cublas:
+                    Ab, Wb = A32.bfloat16(), W32.bfloat16()
+                    for _ in range(a.warmup):
+                        torch.matmul(Ab, Wb.T)
+                    torch.cuda.synchronize()
+                    e0.record()
+                    for _ in range(a.iters):
+                        torch.matmul(Ab, Wb.T)
+                    e1.record()
+                    torch.cuda.synchronize()
+                    cms = e0.elapsed_time(e1) / a.iters
+                    row["cublas_tflops"] = 2.0 * M * N * K / (cms / 1e3) / 1e12
+                    del Ab, Wb
+                rows.append(row)
+                if a.json:
+                    print(json.dumps(row), flush=True)
+                else:
+                    print("M=%6d K=%5d N=%5d %-6s tile=%d %8.3f ms %7.1f TF/s (%.2f sust, %.2f burst) cublas=%s err=%s"
+                          % (M, K, N, mode, bn, ms, tf, tf / sus, tf / burst,
+                             "%.1f" % row["cublas_tflops"] if "cublas_tflops" in row else "-",
+                             "%.2e" % err if err is not None else "-"), flush=True)
+                del A, W, out, resid
+            del A32, W32
+            torch.cuda.empty_cache()
+    return rows
+
+
+if __name__ == "__main__":
+    sys.path.insert(0, ROOT)
+    main()

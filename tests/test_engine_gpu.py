@@ -275,6 +275,22 @@ def test_order_invariance_full_c2(large_bf16):
     assert rel(ac_p, ac[perm]) < 1e-5
 
 
+def test_pair_tile_matches_single_cta_tiles(large_ckpt, large_bf16):
+    """At C2 size the engine runs its GEMMs on the CTA-pair 256 x 256 tile; the single-CTA tiles
+    (LAYA_NO_PAIR_GEMM) must give the same decisions."""
+    qs = workloads.c2(synth.ARCHS["large"], states=16)
+    rc, lo, ac = large_bf16.forward(qs)
+    assert rc == 0
+    h = Handle(large_ckpt, 0, env={"LAYA_MAX_TOKENS": 65536, "LAYA_NO_PAIR_GEMM": 1})
+    try:
+        rc2, lo2, ac2 = h.forward(qs)
+    finally:
+        h.close()
+    assert rc2 == 0
+    assert prob_delta(lo, lo2, qs) < 1e-3
+    assert act_rel(ac, ac2) < 1e-2
+
+
 def test_stage_replay_matches_forward(large_bf16):
     from tests.engine_helpers import FP, IP
     qs = workloads.c2(synth.ARCHS["large"], states=8)

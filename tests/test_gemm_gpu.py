@@ -1,6 +1,7 @@
 """Kernel parity of the tcgen05 GEMM (layamd_b200/csrc/gemm_tc.cu) through the C ABI entry point
 ``laya_b200_gemm``, against a plain PyTorch fp32/fp64 reference of the same op.
 
+bn selects the tile: 128 / 256 (one CTA per 128 x bn tile) or 512 (CTA pair, 256 x 256, 2-SM MMA).
 Tolerances (max|out-ref| / max|ref|): fp32-output bf16 GEMM 1e-4 (fp32 accumulation order only);
 three-product split-bf16 (fp32-parity mode) 5e-5 against fp64 on the fp32 inputs; bf16 outputs 1e-2
 (one bf16 rounding of the result).
@@ -52,7 +53,7 @@ def split(x):
     return torch.stack([hi, lo]).contiguous()
 
 
-@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("bn", [128, 256, 512])
 @pytest.mark.parametrize("M,N,K", [(1, 256, 64), (127, 512, 1024), (300, 1024, 72), (1024, 3072, 1024),
                                    (520, 1024, 2624), (4096, 768, 1152)])
 def test_store_f32(L, bn, M, N, K):
@@ -65,7 +66,7 @@ def test_store_f32(L, bn, M, N, K):
     assert rel(out, ref) < 1e-4
 
 
-@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("bn", [128, 256, 512])
 @pytest.mark.parametrize("M,N,K", [(200, 1024, 1024), (512, 3072, 1024), (333, 1024, 4096)])
 def test_split_bf16_parity(L, bn, M, N, K):
     g = torch.Generator(device="cuda").manual_seed(11 + M)
@@ -107,7 +108,7 @@ def test_bf16x2_planes(L):
     assert rel(out[0].float() + out[1].float(), ref) < 1e-4
 
 
-@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("bn", [128, 256, 512])
 def test_residual(L, bn):
     M, N, K = 777, 1024, 2624
     g = torch.Generator(device="cuda").manual_seed(9)
@@ -127,7 +128,7 @@ def rope_tables(max_pos, theta):
     return torch.cos(f).cuda().contiguous(), torch.sin(f).cuda().contiguous()
 
 
-@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("bn", [128, 256, 512])
 def test_rope(L, bn):
     D, M, K = 256, 300, 256
     N = 3 * D
@@ -161,7 +162,7 @@ def interleave_geglu(W, I, group=64):
     return torch.cat(parts).contiguous()
 
 
-@pytest.mark.parametrize("I,bn", [(2624, 256), (1152, 256), (2624, 128), (192, 256)])
+@pytest.mark.parametrize("I,bn", [(2624, 256), (1152, 256), (2624, 128), (192, 256), (2624, 512), (192, 512)])
 def test_geglu(L, I, bn):
     M, K = 513, 1024
     g = torch.Generator(device="cuda").manual_seed(I)
