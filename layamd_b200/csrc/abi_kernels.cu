@@ -41,11 +41,15 @@ extern "C" int laya_b200_gemm(const void* A, const void* W, void* out, float* re
   const uint32_t box_b = bn == kGemmPair ? 128u : static_cast<uint32_t>(bn);  // a pair tile loads 128 B rows per CTA
   if (!make_operand_map(&tb, W, (uint64_t)K, (uint64_t)N, (uint64_t)planes, box_b)) return -3;
   GemmShape sh{M, N, K, planes == 2 ? 3 : 1};
+  const int ncols = epi == EPI_GEGLU ? geglu_I : N;
+  CUtensorMap tc;
+  const bool f32 = epi == EPI_RESID || out_mode == OUT_F32;
+  void* dst = epi == EPI_RESID ? static_cast<void*>(resid) : out;
+  if (!dst || !make_output_map(&tc, dst, f32, (uint64_t)ncols, (uint64_t)M, f32 ? 1 : (out_mode == OUT_BF16X2 ? 2 : 1)))
+    return -3;
   GemmEpi ep;
   ep.kind = epi;
   ep.out_mode = out_mode;
-  ep.out = out;
-  ep.resid = resid;
   ep.bias = bias;
   ep.act = act;
   ep.cos_t = cos_t;
@@ -53,13 +57,10 @@ extern "C" int laya_b200_gemm(const void* A, const void* W, void* out, float* re
   ep.pos = pos;
   ep.rope_cols = rope_cols;
   ep.geglu_I = geglu_I;
-  const int ncols = epi == EPI_GEGLU ? geglu_I : N;
-  ep.ld = ncols;
-  ep.plane = (long long)M * ncols;
   int* err = err_word(dev);
   if (!err) return -4;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = gemm_launch(ta, tb, bn, sh, ep, err, num_sms(dev), st);
+  cudaError_t e = gemm_launch(ta, tb, tc, bn, sh, ep, err, num_sms(dev), st);
   if (e != cudaSuccess) {
     fprintf(stderr, "[laya] gemm launch: %s\n", cudaGetErrorString(e));
     return -5;

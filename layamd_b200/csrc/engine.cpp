@@ -145,6 +145,8 @@ class Replica {
   float* x = nullptr;
   void* qkv = nullptr;
   Operand xn, ao, mg, ff, xng, aog, ffg, xs;
+  // epilogue output maps (TMA store / reduce-add targets)
+  CUtensorMap out_qkv, out_mg, out_ff, out_ffg, out_x, out_xg, out_hs;
   float* xg = nullptr;
   void* hs = nullptr;
   float *d_logits = nullptr, *d_act = nullptr;
@@ -355,6 +357,14 @@ class Replica {
       return false;
     if (!dalloc(&xg, (size_t)Rcap * D * 4, err)) return false;
     if (!dalloc(reinterpret_cast<char**>(&hs), (size_t)Rcap * D * (P == 2 ? 4 : 2), err)) return false;
+    const bool f32acts = P == 2;  // fp32 qkv / scorer hidden in parity mode
+    if (!make_output_map(&out_qkv, qkv, f32acts, 3 * D, Tcap, 1) || !make_output_map(&out_mg, mg.p, false, I, Tcap, P) ||
+        !make_output_map(&out_ff, ff.p, false, FF, Tcap, P) || !make_output_map(&out_ffg, ffg.p, false, FF, Rcap, P) ||
+        !make_output_map(&out_x, x, true, D, Tcap, 1) || !make_output_map(&out_xg, xg, true, D, Rcap, 1) ||
+        !make_output_map(&out_hs, hs, f32acts, D, Rcap, 1)) {
+      *err = "output tensor map rejected";
+      return false;
+    }
     if (!dalloc(&d_logits, (size_t)Rcap * 4, err)) return false;
     if (!dalloc(&d_act, (size_t)Bcap * cfg.n_act * 4, err)) return false;
     if (!dalloc(&d_err, 16, err)) return false;
@@ -479,27 +489,22 @@ class Replica {
     const long long t256 = (long long)((M + 127) / 128) * ((W.N + 255) / 256);
     return t256 >= 2LL * num_sms ? 256 : 128;
   }
-  void gemm(const Operand& A, int M, const Mat& W, const GemmEpi& ep) {
+  void gemm(const Operand& A, int M, const Mat& W, const CUtensorMap& out, const GemmEpi& ep) {
     const int bn = pick_tile(M, W);
     GemmShape sh{M, W.N, W.K, nseg};
-    launched(gemm_launch(A.map, bn == 256 ? W.m256 : W.m128, bn, sh, ep, d_err, num_sms, st));
+    launched(gemm_launch(A.map, bn == 256 ? W.m256 : W.m128, out, bn, sh, ep, d_err, num_sms, st));
   }
-  GemmEpi epi_store(void* out, long long ld, long long plane, int out_mode, const float* bias, int act) const {
+  GemmEpi epi_store(int out_mode, const float* bias, int act) const {
     GemmEpi e;
     e.kind = EPI_STORE;
-    e.out = out;
-    e.ld = ld;
-    e.plane = plane;
     e.out_mode = out_mode;
     e.bias = bias;
     e.act = act;
     return e;
   }
-  GemmEpi epi_resid(float* xres, long long ld, const float* bias) const {
+  GemmEpi epi_resid(const float* bias) const {
     GemmEpi e;
     e.kind = EPI_RESID;
-    e.resid = xres;
-    e.ld = ld;
     e.bias = bias;
     return e;
   }
@@ -576,18 +581,18 @@ class Replica {
     for (int l = 0; l < NL; ++l) {
       const bool glob = cfg.layer_types[l] == AttnKind::Global;
       stage("gemm_qkv", [&] {
-        GemmEpi e = epi_store(qkv, 3LL * D, 0, qkv_mode, nullptr, ACT_NONE);
+        GemmEpi e = epi_store(qkv_mode, nullptr, ACT_NONE);
         e.kind = EPI_ROPE;
         e.cos_t = glob ? cos_g : cos_l;
         e.sin_t = glob ? sin_g : sin_l;
         e.pos = pos;
         e.rope_cols = 2 * D;
-        gemm(xn, M, enc[l].Wqkv, e);
+        gemm(xn, M, enc[l].Wqkv, out_qkv, e);
       });
       stage(glob ? "attn_global" : "attn_sliding", [&] {
         attend(items, L.items_cap, soff, slen, glob ? 0 : cfg.local_attention / 2, ao.p, ao.plane, nullptr, nullptr);
       });
-      stage("gemm_attn_out", [&] { gemm(ao, M, enc[l].Wo, epi_resid(x, D, nullptr)); });
+      stage("gemm_attn_out", [&] { gemm(ao, M, enc[l].Wo, out_x, epi_resid(nullptr)); });
       stage("ln", [&] {
         LnArgs a = ln_base(M);
         a.src = x;
@@ -597,12 +602,12 @@ class Replica {
         launched(ln_launch(a, st));
       });
       stage("gemm_mlp_in", [&] {
-        GemmEpi e = epi_store(mg.p, I, mg.plane, act_mode(), nullptr, ACT_NONE);
+        GemmEpi e = epi_store(act_mode(), nullptr, ACT_NONE);
         e.kind = EPI_GEGLU;
         e.geglu_I = I;
-        gemm(xn, M, enc[l].Wi, e);
+        gemm(xn, M, enc[l].Wi, out_mg, e);
       });
-      stage("gemm_mlp_out", [&] { gemm(mg, M, enc[l].Wmo, epi_resid(x, D, nullptr)); });
+      stage("gemm_mlp_out", [&] { gemm(mg, M, enc[l].Wmo, out_x, epi_resid(nullptr)); });
       snprintf(nb, sizeof nb, "enc%d", l);
       dump(nb, x, p.T);
       stage("ln", [&] {
@@ -629,10 +634,10 @@ class Replica {
     for (int j = 0; j < HL; ++j) {
       const Head& h = head[j];
       const bool last = j == HL - 1;
-      stage("head_gemm", [&] { gemm(xn, M, h.inW, epi_store(qkv, 3LL * D, 0, qkv_mode, h.inB, ACT_NONE)); });
+      stage("head_gemm", [&] { gemm(xn, M, h.inW, out_qkv, epi_store(qkv_mode, h.inB, ACT_NONE)); });
       if (!last) {
         stage("head_attn", [&] { attend(items, L.items_cap, soff, slen, 0, ao.p, ao.plane, nullptr, nullptr); });
-        stage("head_gemm", [&] { gemm(ao, M, h.outW, epi_resid(x, D, h.outB)); });
+        stage("head_gemm", [&] { gemm(ao, M, h.outW, out_x, epi_resid(h.outB)); });
         stage("head_ln", [&] {
           LnArgs a = ln_base(M);
           a.eps = 1e-5f;
@@ -643,8 +648,8 @@ class Replica {
           a.out_plane = xn.plane;
           launched(ln_launch(a, st));
         });
-        stage("head_gemm", [&] { gemm(xn, M, h.l1W, epi_store(ff.p, FF, ff.plane, act_mode(), h.l1B, ACT_RELU)); });
-        stage("head_gemm", [&] { gemm(ff, M, h.l2W, epi_resid(x, D, h.l2B)); });
+        stage("head_gemm", [&] { gemm(xn, M, h.l1W, out_ff, epi_store(act_mode(), h.l1B, ACT_RELU)); });
+        stage("head_gemm", [&] { gemm(ff, M, h.l2W, out_x, epi_resid(h.l2B)); });
         stage("head_ln", [&] {
           LnArgs a = ln_base(M);
           a.eps = 1e-5f;
@@ -667,7 +672,7 @@ class Replica {
           a.out_f32 = xg;
           launched(ln_launch(a, st));
         });
-        stage("head_gemm", [&] { gemm(aog, R, h.outW, epi_resid(xg, D, h.outB)); });
+        stage("head_gemm", [&] { gemm(aog, R, h.outW, out_xg, epi_resid(h.outB)); });
         stage("head_ln", [&] {
           LnArgs a = ln_base(R);
           a.eps = 1e-5f;
@@ -678,8 +683,8 @@ class Replica {
           a.out_plane = xng.plane;
           launched(ln_launch(a, st));
         });
-        stage("head_gemm", [&] { gemm(xng, R, h.l1W, epi_store(ffg.p, FF, ffg.plane, act_mode(), h.l1B, ACT_RELU)); });
-        stage("head_gemm", [&] { gemm(ffg, R, h.l2W, epi_resid(xg, D, h.l2B)); });
+        stage("head_gemm", [&] { gemm(xng, R, h.l1W, out_ffg, epi_store(act_mode(), h.l1B, ACT_RELU)); });
+        stage("head_gemm", [&] { gemm(ffg, R, h.l2W, out_xg, epi_resid(h.l2B)); });
         snprintf(nb, sizeof nb, "head%d", j);
         dump(nb, xg, R);
       }
@@ -693,7 +698,7 @@ class Replica {
       a.out_bf = xs.p;
       a.out_plane = xs.plane;
       launched(ln_launch(a, st));
-      gemm(xs, KT, sc1, epi_store(hs, D, 0, P == 2 ? OUT_F32 : OUT_BF16, sc1B, ACT_GELU));
+      gemm(xs, KT, sc1, out_hs, epi_store(P == 2 ? OUT_F32 : OUT_BF16, sc1B, ACT_GELU));
     });
     stage("head_out", [&] {
       HeadOutArgs a;

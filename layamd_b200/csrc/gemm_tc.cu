@@ -32,6 +32,7 @@ template <int BN, int STAGES>
 struct GemmSmem {
   alignas(1024) bf16 a[STAGES][kBM * kBK];
   alignas(1024) bf16 b[STAGES][BN * kBK];
+  alignas(1024) uint8_t stg[4][8192];  // epilogue staging: two 32-row x 128-byte tiles per epilogue warp
   alignas(8) uint64_t full[STAGES];
   uint64_t empty[STAGES];
   uint64_t accf[2];
@@ -39,7 +40,6 @@ struct GemmSmem {
   uint64_t drain;
   uint32_t tmem;
   int abort;
-  alignas(16) float stg[4][32 * 32];  // epilogue staging, one 32 x 32 fp32 tile per epilogue warp
 };
 
 template <int BN>
@@ -53,80 +53,92 @@ __device__ __forceinline__ float apply_act(float v, int act) {
   return v;
 }
 
-// Per-warp staging tile of the epilogue: 32 rows x 32 fp32, 16-byte chunks XOR-swizzled by row, so
-// both the row-per-thread writes (after tcgen05.ld) and the row-segment reads are bank-conflict free.
-__device__ __forceinline__ float* stg_at(float* stg, int r, int f) { return stg + r * 32 + ((f ^ (r & 7)) << 2); }
+// ---- epilogue output path: per-warp double-buffered 32-row staging tiles (4 KB each, 128-byte rows
+// in the 128-byte swizzle) written one row per thread, then stored (or reduce-added) to global
+// memory by one TMA bulk-tensor operation issued by lane 0. A buffer is reused only after the store
+// issued from it two rounds earlier has finished reading shared memory.
+struct Stager {
+  uint8_t* base;  // 8 KB, 1024-byte aligned
+  int buf;
+};
 
-__device__ __forceinline__ void stage_row(float* stg, int lane, const float (&v)[32]) {
-#pragma unroll
-  for (int f = 0; f < 8; ++f)
-    *reinterpret_cast<float4*>(stg_at(stg, lane, f)) = make_float4(v[4 * f], v[4 * f + 1], v[4 * f + 2], v[4 * f + 3]);
+__device__ __forceinline__ uint8_t* stg_acquire(Stager& s, int lane) {
+  if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+  __syncwarp();
+  return s.base + s.buf * 4096;
 }
 
-// Coalesced write-out of one staged 32 x 32 chunk (rows row0.., columns col..col+31): lane l handles
-// 16 bytes (float4 l%8) of rows l/8 + 4k, so every warp instruction covers four 128-byte row
-// segments. `post` adds the bias and applies the activation; `resid` adds into the fp32 residual.
-template <bool RESID>
-__device__ __forceinline__ void write_chunk(float* stg, int lane, int row0, int col, const GemmShape& sh,
-                                            const GemmEpi& ep, bool post) {
-  const int f = lane & 7, j = lane >> 3;
-  float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (post && ep.bias) b4 = *reinterpret_cast<const float4*>(ep.bias + col + 4 * f);
-  float4 v[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    v[k] = *reinterpret_cast<const float4*>(stg_at(stg, 4 * k + j, f));
-    if (post) {
-      v[k].x += b4.x; v[k].y += b4.y; v[k].z += b4.z; v[k].w += b4.w;
-      if (ep.act != ACT_NONE) {
-        v[k].x = apply_act(v[k].x, ep.act); v[k].y = apply_act(v[k].y, ep.act);
-        v[k].z = apply_act(v[k].z, ep.act); v[k].w = apply_act(v[k].w, ep.act);
-      }
-    }
+__device__ __forceinline__ void stg_issue(Stager& s, int lane, const CUtensorMap* map, int col, int row, int plane,
+                                          bool reduce_add) {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy writes -> TMA reads
+  __syncwarp();
+  if (lane == 0) {
+    const uint32_t src = smem_u32(s.base + s.buf * 4096);
+    if (reduce_add)
+      asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];"
+                   ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(col), "r"(row), "r"(plane)
+                   : "memory");
+    else
+      asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];"
+                   ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(col), "r"(row), "r"(plane)
+                   : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
   }
-  if constexpr (RESID) {
-    float4 x[8];
+  s.buf ^= 1;
+}
+
+__device__ __forceinline__ void stg_drain(int lane) {
+  if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  __syncwarp();
+}
+
+// Row `lane` of a 32 x 64 bf16 tile / 32 x 32 fp32 tile, 16-byte chunk j at (j ^ (lane % 8)).
+__device__ __forceinline__ void put_bf16_row(uint8_t* tile, int lane, const float* v) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {  // all loads first: eight independent 16-byte requests in flight
-      const int row = row0 + 4 * k + j;
-      if (row < sh.M) x[k] = *reinterpret_cast<const float4*>(ep.resid + (long long)row * ep.ld + col + 4 * f);
-    }
+  for (int j = 0; j < 8; ++j) {
+    const uint4 q = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                               pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+    *reinterpret_cast<uint4*>(tile + lane * 128 + ((j ^ (lane & 7)) << 4)) = q;
+  }
+}
+__device__ __forceinline__ void put_f32_row(uint8_t* tile, int lane, const float* v) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int row = row0 + 4 * k + j;
-      if (row < sh.M) {
-        x[k].x += v[k].x; x[k].y += v[k].y; x[k].z += v[k].z; x[k].w += v[k].w;
-        *reinterpret_cast<float4*>(ep.resid + (long long)row * ep.ld + col + 4 * f) = x[k];
-      }
-    }
-  } else {
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<float4*>(tile + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+
+// 64 consecutive output columns of the warp's 32 rows: one bf16 box (plus the lo plane in
+// OUT_BF16X2 mode), or two fp32 boxes.
+__device__ __forceinline__ void emit64(Stager& s, int lane, const CUtensorMap* map, int mode, float (&v)[64], int col,
+                                       int row0) {
+  if (mode == OUT_F32) {
+    uint8_t* t = stg_acquire(s, lane);
+    put_f32_row(t, lane, v);
+    stg_issue(s, lane, map, col, row0, 0, false);
+    t = stg_acquire(s, lane);
+    put_f32_row(t, lane, v + 32);
+    stg_issue(s, lane, map, col + 32, row0, 0, false);
+    return;
+  }
+  uint8_t* t = stg_acquire(s, lane);
+  put_bf16_row(t, lane, v);
+  stg_issue(s, lane, map, col, row0, 0, false);
+  if (mode == OUT_BF16X2) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int row = row0 + 4 * k + j;
-      if (row >= sh.M) continue;
-      const long long off = (long long)row * ep.ld + col + 4 * f;
-      if (ep.out_mode == OUT_F32) {
-        *reinterpret_cast<float4*>(static_cast<float*>(ep.out) + off) = v[k];
-      } else {
-        bf16* base = static_cast<bf16*>(ep.out);
-        const uint32_t h0 = pack_bf16x2(v[k].x, v[k].y), h1 = pack_bf16x2(v[k].z, v[k].w);
-        *reinterpret_cast<uint2*>(base + off) = make_uint2(h0, h1);
-        if (ep.out_mode == OUT_BF16X2) {
-          const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h0));
-          const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h1));
-          *reinterpret_cast<uint2*>(base + ep.plane + off) =
-              make_uint2(pack_bf16x2(v[k].x - f0.x, v[k].y - f0.y), pack_bf16x2(v[k].z - f1.x, v[k].w - f1.y));
-        }
-      }
-    }
+    for (int i = 0; i < 64; ++i) v[i] -= __bfloat162float(__float2bfloat16_rn(v[i]));
+    t = stg_acquire(s, lane);
+    put_bf16_row(t, lane, v);
+    stg_issue(s, lane, map, col, row0, 1, false);
   }
 }
 
 // Epilogue of one tile for one warp (32 rows starting at row0; thread `lane` holds row row0+lane
-// after each tcgen05.ld). Every tcgen05.ld is executed by the whole warp; rows >= M are never stored.
+// after each tcgen05.ld). Every tcgen05.ld is executed by the whole warp. Output boxes are clipped by
+// the TMA unit at the row extent of the output map.
 template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row0, int lane, int nb, const GemmShape& sh,
-                                              const GemmEpi& ep, float* stg) {
+                                              const GemmEpi& ep, const CUtensorMap* out_map, Stager& stg) {
   const int row = row0 + lane;
   const bool valid = row < sh.M;
   if constexpr (EPI == EPI_GEGLU) {
@@ -134,17 +146,17 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row0, int lane
     for (int s = 0; s < BN; s += 128) {
       const int ocol = nb * (BN / 2) + s / 2;  // first output column of this 128-column group
       if (ocol >= ep.geglu_I) break;
+      float v[64];
+#pragma unroll
       for (int c = 0; c < 64; c += 32) {
         float xin[32], gate[32];
         __syncwarp();
         tmem_ld32(tbase + s + c, xin);
         tmem_ld32(tbase + s + 64 + c, gate);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) xin[i] = gelu_erf(xin[i]) * gate[i];
-        stage_row(stg, lane, xin);
-        __syncwarp();
-        write_chunk<false>(stg, lane, row0, ocol + c, sh, ep, false);
+        for (int i = 0; i < 32; ++i) v[c + i] = gelu_erf(xin[i]) * gate[i];
       }
+      emit64(stg, lane, out_map, ep.out_mode, v, ocol, row0);
     }
   } else if constexpr (EPI == EPI_ROPE) {
     // cos/sin of this row's position are the same for every head: load them once per tile, as
@@ -165,40 +177,58 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row0, int lane
     for (int h = 0; h < BN; h += 64) {
       const int col = nb * BN + h;
       if (col >= sh.N) break;
-      float x1[32], x2[32];
+      float v[64];
       __syncwarp();
-      tmem_ld32(tbase + h, x1);
-      tmem_ld32(tbase + h + 32, x2);
+      tmem_ld32(tbase + h, *reinterpret_cast<float(*)[32]>(v));
+      tmem_ld32(tbase + h + 32, *reinterpret_cast<float(*)[32]>(v + 32));
       if (ep.bias) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) { x1[i] += ep.bias[col + i]; x2[i] += ep.bias[col + 32 + i]; }
+        for (int i = 0; i < 64; ++i) v[i] += ep.bias[col + i];
       }
       if (valid && col < ep.rope_cols) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float a = x1[i], b = x2[i];
-          x1[i] = a * cs[i] - b * sn[i];
-          x2[i] = b * cs[i] + a * sn[i];
+          const float a = v[i], b = v[32 + i];
+          v[i] = a * cs[i] - b * sn[i];
+          v[32 + i] = b * cs[i] + a * sn[i];
         }
       }
-      stage_row(stg, lane, x1);
-      __syncwarp();
-      write_chunk<false>(stg, lane, row0, col, sh, ep, false);
-      __syncwarp();
-      stage_row(stg, lane, x2);
-      __syncwarp();
-      write_chunk<false>(stg, lane, row0, col + 32, sh, ep, false);
+      emit64(stg, lane, out_map, ep.out_mode, v, col, row0);
     }
-  } else {
+  } else if constexpr (EPI == EPI_RESID) {
+    // x += acc (+ bias) as a TMA reduce-add of 32 x 32 fp32 boxes: the read-modify-write of the
+    // residual happens in L2, never in registers.
     for (int c = 0; c < BN; c += 32) {
       const int col = nb * BN + c;
       if (col >= sh.N) break;
       float v[32];
       __syncwarp();
       tmem_ld32(tbase + c, v);
-      stage_row(stg, lane, v);
+      if (ep.bias) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += ep.bias[col + i];
+      }
+      uint8_t* t = stg_acquire(stg, lane);
+      put_f32_row(t, lane, v);
+      stg_issue(stg, lane, out_map, col, row0, 0, true);
+    }
+  } else {
+    for (int c = 0; c < BN; c += 64) {
+      const int col = nb * BN + c;
+      if (col >= sh.N) break;
+      float v[64];
       __syncwarp();
-      write_chunk<EPI == EPI_RESID>(stg, lane, row0, col, sh, ep, true);
+      tmem_ld32(tbase + c, *reinterpret_cast<float(*)[32]>(v));
+      tmem_ld32(tbase + c + 32, *reinterpret_cast<float(*)[32]>(v + 32));  // N is a multiple of 64 here
+      if (ep.bias) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] += ep.bias[col + i];
+      }
+      if (ep.act != ACT_NONE) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] = apply_act(v[i], ep.act);
+      }
+      emit64(stg, lane, out_map, ep.out_mode, v, col, row0);
     }
   }
 }
@@ -206,7 +236,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row0, int lane
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-                   const GemmShape sh, const GemmEpi ep, int* err) {
+                   const __grid_constant__ CUtensorMap tc, const GemmShape sh, const GemmEpi ep, int* err) {
   constexpr int STAGES = StagesFor<BN>::value;
   constexpr uint32_t kIdesc = idesc_bf16(kBM, BN);
   constexpr uint32_t kStageBytes = (kBM + BN) * kBK * 2;
@@ -227,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     S.abort = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) { tma_prefetch_desc(&ta); tma_prefetch_desc(&tb); }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&ta); tma_prefetch_desc(&tb); tma_prefetch_desc(&tc); }
   if (warp == 1) { tmem_alloc(smem_u32(&S.tmem), 2 * BN); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
@@ -308,27 +338,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue warps 2..5; warp w may only touch TMEM lanes 32*(w%4) .. +31
     const int q = warp & 3;
+    Stager stager{S.stg[q], 0};
     int local = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t accph = (local >> 1) & 1;
       const int mb = t / num_n, nb = t - (t / num_n) * num_n;
       const int row = mb * kBM + q * 32 + lane;
-      if constexpr (EPI == EPI_RESID) {
-        // pull this tile's residual rows into L2 while its main loop is still running
-        if (row < sh.M) {
-          const int cols = min(BN, sh.N - nb * BN);
-          prefetch_l2_bulk(ep.resid + (long long)row * ep.ld + nb * BN, static_cast<uint32_t>(cols) * 4u);
-        }
-      }
       if (!mbar_wait(smem_u32(&S.accf[acc]), accph, abort, err, kErrGemmAccFull)) break;
       tc_fence_after();
       const uint32_t tbase = tmem + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue_tile<BN, EPI>(tbase, mb * kBM + q * 32, lane, nb, sh, ep, S.stg[q]);
+      epilogue_tile<BN, EPI>(tbase, mb * kBM + q * 32, lane, nb, sh, ep, &tc, stager);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&S.acce[acc]));
     }
+    stg_drain(lane);  // output stores finished before the CTA can exit
   }
 
   tc_fence_before();
@@ -352,6 +377,7 @@ constexpr int kPairStages = 6;
 struct GemmSmemPair {
   alignas(1024) bf16 a[kPairStages][128 * kBK];
   alignas(1024) bf16 b[kPairStages][128 * kBK];
+  alignas(1024) uint8_t stg[4][8192];
   alignas(8) uint64_t full[kPairStages];
   uint64_t empty[kPairStages];
   uint64_t accf[2];
@@ -359,14 +385,13 @@ struct GemmSmemPair {
   uint64_t drain;
   uint32_t tmem;
   int abort;
-  alignas(16) float stg[4][32 * 32];
 };
 constexpr size_t gemm_pair_smem_bytes() { return sizeof(GemmSmemPair) + 1024; }
 
 template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-                        const GemmShape sh, const GemmEpi ep, int* err) {
+                        const __grid_constant__ CUtensorMap tc, const GemmShape sh, const GemmEpi ep, int* err) {
   constexpr int BN = 256;
   constexpr uint32_t kIdesc = idesc_bf16(256, BN);
   constexpr uint32_t kPairStageBytes = 2u * (128 + 128) * kBK * 2;  // both CTAs' A and B halves
@@ -389,7 +414,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     S.abort = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) { tma_prefetch_desc(&ta); tma_prefetch_desc(&tb); }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&ta); tma_prefetch_desc(&tb); tma_prefetch_desc(&tc); }
   if (warp == 1) { tmem_alloc_pair(smem_u32(&S.tmem), 2 * BN); tmem_relinquish_pair(); }
   tc_fence_before();
   cluster_sync_all();  // both CTAs' barriers are initialised before any cross-CTA signal
@@ -464,6 +489,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else {
     const int q = warp & 3;
+    Stager stager{S.stg[q], 0};
     const uint32_t acce_leader0 = mapa_shared(smem_u32(&S.acce[0]), 0);
     const uint32_t acce_leader1 = mapa_shared(smem_u32(&S.acce[1]), 0);
     int local = 0;
@@ -472,20 +498,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t accph = (local >> 1) & 1;
       const int mb = t / num_n, nb = t - (t / num_n) * num_n;
       const int row0 = mb * 256 + (int)rank * 128 + q * 32;
-      if constexpr (EPI == EPI_RESID) {
-        if (row0 + lane < sh.M) {
-          const int cols = min(BN, sh.N - nb * BN);
-          prefetch_l2_bulk(ep.resid + (long long)(row0 + lane) * ep.ld + nb * BN, static_cast<uint32_t>(cols) * 4u);
-        }
-      }
       if (!mbar_wait(smem_u32(&S.accf[acc]), accph, abort, err, kErrGemmAccFull)) break;
       tc_fence_after();
       const uint32_t tbase = tmem + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue_tile<BN, EPI>(tbase, row0, lane, nb, sh, ep, S.stg[q]);
+      epilogue_tile<BN, EPI>(tbase, row0, lane, nb, sh, ep, &tc, stager);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? acce_leader1 : acce_leader0);
     }
+    stg_drain(lane);
   }
 
   tc_fence_before();
@@ -521,24 +542,24 @@ cudaError_t prepare_one() {
 }
 
 template <int BN, int EPI>
-cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmShape& sh, const GemmEpi& ep,
-                       int* err, int grid_ctas, cudaStream_t st) {
+cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmShape& sh,
+                       const GemmEpi& ep, int* err, int grid_ctas, cudaStream_t st) {
   constexpr size_t smem = gemm_smem_bytes<BN>();
   const int tiles = ((sh.M + kBM - 1) / kBM) * ((sh.N + BN - 1) / BN);
   const int grid = tiles < grid_ctas ? tiles : grid_ctas;
   if (grid <= 0) return cudaSuccess;
-  gemm_tc_kernel<BN, EPI><<<grid, kThreads, smem, st>>>(ta, tb, sh, ep, err);
+  gemm_tc_kernel<BN, EPI><<<grid, kThreads, smem, st>>>(ta, tb, tc, sh, ep, err);
   return cudaGetLastError();
 }
 
 template <int BN>
-cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmShape& sh, const GemmEpi& ep,
-                      int* err, int grid_ctas, cudaStream_t st) {
+cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmShape& sh,
+                      const GemmEpi& ep, int* err, int grid_ctas, cudaStream_t st) {
   switch (ep.kind) {
-    case EPI_STORE: return launch_one<BN, EPI_STORE>(ta, tb, sh, ep, err, grid_ctas, st);
-    case EPI_ROPE: return launch_one<BN, EPI_ROPE>(ta, tb, sh, ep, err, grid_ctas, st);
-    case EPI_GEGLU: return launch_one<BN, EPI_GEGLU>(ta, tb, sh, ep, err, grid_ctas, st);
-    case EPI_RESID: return launch_one<BN, EPI_RESID>(ta, tb, sh, ep, err, grid_ctas, st);
+    case EPI_STORE: return launch_one<BN, EPI_STORE>(ta, tb, tc, sh, ep, err, grid_ctas, st);
+    case EPI_ROPE: return launch_one<BN, EPI_ROPE>(ta, tb, tc, sh, ep, err, grid_ctas, st);
+    case EPI_GEGLU: return launch_one<BN, EPI_GEGLU>(ta, tb, tc, sh, ep, err, grid_ctas, st);
+    case EPI_RESID: return launch_one<BN, EPI_RESID>(ta, tb, tc, sh, ep, err, grid_ctas, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -563,12 +584,12 @@ cudaError_t prepare_pair(int* clusters) {
 }
 
 template <int EPI>
-cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmShape& sh, const GemmEpi& ep, int* err,
-                        int clusters, cudaStream_t st) {
+cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmShape& sh,
+                        const GemmEpi& ep, int* err, int clusters, cudaStream_t st) {
   const int tiles = ((sh.M + 255) / 256) * ((sh.N + 255) / 256);
   const int ncl = tiles < clusters ? tiles : clusters;
   if (ncl <= 0) return cudaSuccess;
-  gemm_tc_pair_kernel<EPI><<<2 * ncl, kThreads, gemm_pair_smem_bytes(), st>>>(ta, tb, sh, ep, err);
+  gemm_tc_pair_kernel<EPI><<<2 * ncl, kThreads, gemm_pair_smem_bytes(), st>>>(ta, tb, tc, sh, ep, err);
   return cudaGetLastError();
 }
 
@@ -595,6 +616,21 @@ bool make_operand_map(CUtensorMap* map, const void* base, uint64_t K, uint64_t r
   return r == CUDA_SUCCESS;
 }
 
+bool make_output_map(CUtensorMap* map, const void* base, bool f32, uint64_t ld, uint64_t rows, uint64_t planes) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const uint64_t es = f32 ? 4 : 2;
+  if ((ld * es) % 16 != 0 || (reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
+  cuuint64_t dims[3] = {ld, rows, planes};
+  cuuint64_t strides[2] = {ld * es, ld * es * rows};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / es), 32, 1};  // 128-byte rows, 32 rows
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 cudaError_t gemm_prepare_device() {
   cudaError_t e = cudaSuccess;
   for (cudaError_t r : {prepare_one<128, EPI_STORE>(), prepare_one<128, EPI_ROPE>(), prepare_one<128, EPI_GEGLU>(),
@@ -612,24 +648,23 @@ cudaError_t gemm_prepare_device() {
   return e;
 }
 
-cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, int bn, const GemmShape& sh,
-                        const GemmEpi& ep, int* err, int grid_ctas, cudaStream_t st) {
+cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, int bn,
+                        const GemmShape& sh, const GemmEpi& ep, int* err, int grid_ctas, cudaStream_t st) {
   if (sh.M <= 0) return cudaSuccess;
-  if (sh.N % 32 != 0 || sh.K % 8 != 0 || (sh.nseg != 1 && sh.nseg != 3)) return cudaErrorInvalidValue;
+  if (sh.N % 64 != 0 || sh.K % 8 != 0 || (sh.nseg != 1 && sh.nseg != 3)) return cudaErrorInvalidValue;
   if (ep.kind == EPI_GEGLU && (ep.geglu_I % 64 != 0 || sh.N != 2 * ep.geglu_I)) return cudaErrorInvalidValue;
   if (ep.kind == EPI_ROPE && (ep.rope_cols % 64 != 0 || !ep.pos || !ep.cos_t || !ep.sin_t))
     return cudaErrorInvalidValue;
-  if (ep.kind == EPI_RESID ? ep.resid == nullptr : ep.out == nullptr) return cudaErrorInvalidValue;
-  if (bn == 256) return launch_bn<256>(ta, tb, sh, ep, err, grid_ctas, st);
-  if (bn == 128) return launch_bn<128>(ta, tb, sh, ep, err, grid_ctas, st);
+  if (bn == 256) return launch_bn<256>(ta, tb, tc, sh, ep, err, grid_ctas, st);
+  if (bn == 128) return launch_bn<128>(ta, tb, tc, sh, ep, err, grid_ctas, st);
   if (bn == kGemmPair) {
     const int clusters = std::min(gemm_pair_clusters(), grid_ctas / 2);
     if (clusters <= 0) return cudaErrorInvalidConfiguration;
     switch (ep.kind) {
-      case EPI_STORE: return launch_pair<EPI_STORE>(ta, tb, sh, ep, err, clusters, st);
-      case EPI_ROPE: return launch_pair<EPI_ROPE>(ta, tb, sh, ep, err, clusters, st);
-      case EPI_GEGLU: return launch_pair<EPI_GEGLU>(ta, tb, sh, ep, err, clusters, st);
-      case EPI_RESID: return launch_pair<EPI_RESID>(ta, tb, sh, ep, err, clusters, st);
+      case EPI_STORE: return launch_pair<EPI_STORE>(ta, tb, tc, sh, ep, err, clusters, st);
+      case EPI_ROPE: return launch_pair<EPI_ROPE>(ta, tb, tc, sh, ep, err, clusters, st);
+      case EPI_GEGLU: return launch_pair<EPI_GEGLU>(ta, tb, tc, sh, ep, err, clusters, st);
+      case EPI_RESID: return launch_pair<EPI_RESID>(ta, tb, tc, sh, ep, err, clusters, st);
     }
   }
   return cudaErrorInvalidValue;

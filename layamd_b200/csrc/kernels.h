@@ -21,18 +21,17 @@ enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2 };
 
 struct GemmShape {
   int M;     // rows of A that are valid (rows beyond are computed from whatever the buffer holds and never stored)
-  int N;     // rows of B (for EPI_GEGLU: 2*I, interleaved as [64 input rows, their 64 gate rows]...)
+  int N;     // rows of B, a multiple of 64 (for EPI_GEGLU: 2*I, interleaved as [64 input rows, their 64 gate rows]...)
   int K;     // reduction length of one segment
   int nseg;  // 1 (bf16) or 3 (split-bf16 fp32 emulation)
 };
 
+// The epilogue writes through the output tensor map `tc` of gemm_launch (make_output_map): bf16
+// planes for OUT_BF16 / OUT_BF16X2 (plane 1 = lo part), fp32 for OUT_F32 and for EPI_RESID, whose
+// result is added into the existing contents (x += acc) by TMA reduce-add.
 struct GemmEpi {
   int kind = EPI_STORE;
   int out_mode = OUT_BF16;
-  void* out = nullptr;         // EPI_STORE / EPI_ROPE / EPI_GEGLU output base
-  long long ld = 0;            // output (or residual) row stride in elements
-  long long plane = 0;         // plane stride in elements (OUT_BF16X2)
-  float* resid = nullptr;      // EPI_RESID: fp32 [M, ld], updated in place
   const float* bias = nullptr; // [N] fp32, optional
   int act = ACT_NONE;
   const float* cos_t = nullptr;  // EPI_ROPE: [max_pos, 32] tables for this layer's theta
@@ -41,6 +40,10 @@ struct GemmEpi {
   int rope_cols = 0;             // EPI_ROPE: rotate columns [0, rope_cols) (q and k), head dim 64
   int geglu_I = 0;               // EPI_GEGLU: output width I (a multiple of 64)
 };
+
+// Output map of the GEMM epilogue over [planes][rows][ld] (bf16) or [rows][ld] (fp32, planes 1):
+// {32 rows x 128 bytes} boxes with the 128-byte swizzle. Rows beyond `rows` are never written.
+bool make_output_map(CUtensorMap* map, const void* base, bool f32, uint64_t ld, uint64_t rows, uint64_t planes);
 
 // Builds a 3-D tensor map {K, rows, planes} over a bf16 operand with a {64, box_rows, 1} box and the
 // 128-byte swizzle. Returns false if the driver rejects it (alignment).
@@ -58,8 +61,8 @@ constexpr int kGemmPair = 512;
 int gemm_pair_clusters();
 
 // `grid_ctas` caps the persistent grid (CTAs; a pair counts as two).
-cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, int bn, const GemmShape& sh,
-                        const GemmEpi& ep, int* err, int grid_ctas, cudaStream_t st);
+cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, int bn,
+                        const GemmShape& sh, const GemmEpi& ep, int* err, int grid_ctas, cudaStream_t st);
 
 // ------------------------------------------------------------------ attention
 // Work item of the attention kernels: 64 query rows of one sequence.
