@@ -197,8 +197,20 @@ def profiled_gemm_time(L, h, lens, ids, nmark, markers, qtypes, n_act, calls=2):
     return out
 
 
+def all_host_threads():
+    """BLAS pools sized to every host core (torchrun sets OMP_NUM_THREADS=1 for its workers)."""
+    n = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(n)
+    except Exception:
+        pass
+    return n
+
+
 def cpu_sample_rate(qs, arch_name, budget_s=15.0, max_q=48):
     """Decisions/s of the oracle (numpy fp32, all host threads) on the first questions of the batch."""
+    all_host_threads()
     from oracle import model as om
     ck = synth.checkpoint(arch_name, 0)
     o = om.Oracle(synth.load_weights(ck), synth.load_arch(ck))
@@ -218,13 +230,13 @@ def cpu_sample_rate(qs, arch_name, budget_s=15.0, max_q=48):
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
+    cores = all_host_threads()
     arch = synth.ARCHS["large"]
     qs = workloads.c2(arch, seed=1)
     from oracle import model as om
     ck = synth.checkpoint("large", 0)
     o = om.Oracle(synth.load_weights(ck), synth.load_arch(ck))
     per_step = 6  # bounded sample: 2 states x 3 questions per step
-    cores = os.cpu_count()
     for s in range(args.warmup):
         for q in qs[:per_step]:
             o.forward_one(q["ids"], q["markers"], q["qtype"])

@@ -84,6 +84,10 @@ int laya_plan_passes(void* h, int B, const int* lens, const int* nmark, const in
 int laya_plan_passes_cfg(int max_len, int pass_tokens, int max_seqs, int B, const int* lens, const int* nmark,
                          const int* markers, int cap, int* pass_first, int* pass_count, int* pass_rows);
 
+/* The replica (0..ndev-1) each of B questions goes to when a call is sharded over ndev GPUs, as
+ * laya_forward_batch does it; host-only. Returns 0 or -1. */
+int laya_shard_plan(int ndev, int B, const int* lens, int* owner);
+
 /* Benchmark support: validates, packs and uploads one batch (it must fit one pass per device) and
  * keeps it resident; laya_replay then runs the staged pass `iters` times back to back on every
  * device with the inputs already in HBM and writes the device time of the slowest device, measured
@@ -116,6 +120,16 @@ int laya_set_dump_dir(void* h, const char* dir);
 int laya_b200_gemm(const void* A, const void* W, void* out, float* resid, const float* bias, int M, int N, int K,
                    int planes, int epi, int out_mode, int act, int bn, const float* cos_t, const float* sin_t,
                    const int* pos, int rope_cols, int geglu_I, void* stream, int sync);
+
+/* laya_b200_gemm with the K loop split into `splits` slices (1..8) run by different CTAs, for small M
+ * where the output tiles alone cannot fill the GPU (one-CTA tiles, bn 128 or 256). The fp32 partials
+ * go to a workspace the library allocates on the device and keeps for later calls; the last slice
+ * of each tile sums them in slice order, so results do not depend on scheduling. Calls that overlap
+ * on the GPU (other streams) share that workspace and must not be issued. */
+int laya_b200_gemm_splitk(const void* A, const void* W, void* out, float* resid, const float* bias, int M, int N,
+                          int K, int planes, int epi, int out_mode, int act, int bn, const float* cos_t,
+                          const float* sin_t, const int* pos, int rope_cols, int geglu_I, int splits, void* stream,
+                          int sync);
 
 #ifdef __cplusplus
 }

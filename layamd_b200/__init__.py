@@ -52,6 +52,7 @@ def load_lib(path: str = LIB_PATH) -> ctypes.CDLL:
         "laya_prof_get": (i, [vp, ctypes.c_char_p, ctypes.POINTER(d), ctypes.POINTER(ctypes.c_longlong)]),
         "laya_plan_passes": (i, [vp, i, _IP, _IP, _IP, i, _IP, _IP, _IP]),
         "laya_plan_passes_cfg": (i, [i, i, i, i, _IP, _IP, _IP, i, _IP, _IP, _IP]),
+        "laya_shard_plan": (i, [i, i, _IP, _IP]),
         "laya_stage": (i, [vp, i, _IP, _IP, _IP, _IP, _IP]),
         "laya_replay": (i, [vp, i, ctypes.POINTER(d)]),
         "laya_staged_results": (i, [vp, _FP, _FP]),
@@ -59,6 +60,7 @@ def load_lib(path: str = LIB_PATH) -> ctypes.CDLL:
         "laya_io_stats": (i, [vp, ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_longlong),
                               ctypes.POINTER(ctypes.c_longlong), i]),
         "laya_b200_gemm": (i, [vp, vp, vp, vp, vp, i, i, i, i, i, i, i, i, vp, vp, vp, i, i, vp, i]),
+        "laya_b200_gemm_splitk": (i, [vp, vp, vp, vp, vp, i, i, i, i, i, i, i, i, vp, vp, vp, i, i, i, vp, i]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -107,6 +107,12 @@ int laya_plan_passes(void* h, int B, const int* lens, const int* nmark, const in
   return (int)plans.size();
 }
 
+int laya_shard_plan(int ndev, int B, const int* lens, int* owner) {
+  if (ndev < 1 || B < 0 || (B > 0 && (!lens || !owner))) return -1;
+  laya::shard_owners(B, lens, ndev, owner);
+  return 0;
+}
+
 int laya_stage(void* h, int B, const int* lens, const int* ids, const int* nmark, const int* markers,
                const int* qtypes) {
   if (!h || B < 0 || (B > 0 && (!lens || !ids || !nmark || !markers || !qtypes))) return -1;

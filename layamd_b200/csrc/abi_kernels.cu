@@ -1,52 +1,61 @@
 // Kernel-level C entry points: the encoder GEMM on caller-owned device buffers, used by the GEMM
 // sweep (isolated encoder-GEMM benchmark) and by the kernel parity tests. They are additions to
 // the reference ABI; the engine itself never calls them.
-#include "kernels.h"
-#include "laya_api.h"
 #include <cstdio>
 #include <mutex>
 #include <vector>
 
+#include "kernels.h"
+#include "laya_api.h"
+
 namespace {
 std::mutex g_mu;
-std::vector<int*> g_err;  // one device error word per device
-int* err_word(int dev) {
-  std::lock_guard<std::mutex> lk(g_mu);
-  if ((int)g_err.size() <= dev) g_err.resize(dev + 1, nullptr);
-  if (!g_err[dev]) {
+struct DevState {
+  int* err = nullptr;        // device error word
+  float* ws = nullptr;       // split-K partials (grown on demand)
+  size_t ws_floats = 0;
+  int* counters = nullptr;   // split-K tile counters (grown on demand, kept zero)
+  size_t n_counters = 0;
+};
+std::vector<DevState> g_dev;
+
+DevState* dev_state(int dev) {
+  if ((int)g_dev.size() <= dev) g_dev.resize(dev + 1);
+  DevState& d = g_dev[dev];
+  if (!d.err) {
     if (laya::gemm_prepare_device() != cudaSuccess) return nullptr;
-    if (cudaMalloc(&g_err[dev], sizeof(int)) != cudaSuccess) return nullptr;
-    cudaMemset(g_err[dev], 0, sizeof(int));
+    if (cudaMalloc(&d.err, sizeof(int)) != cudaSuccess) return nullptr;
+    cudaMemset(d.err, 0, sizeof(int));
   }
-  return g_err[dev];
+  return &d;
 }
 int num_sms(int dev) {
   int n = 0;
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   return n > 0 ? n : 1;
 }
-}  // namespace
 
-extern "C" int laya_b200_gemm(const void* A, const void* W, void* out, float* resid, const float* bias, int M,
-                              int N, int K, int planes, int epi, int out_mode, int act, int bn,
-                              const float* cos_t, const float* sin_t, const int* pos, int rope_cols,
-                              int geglu_I, void* stream, int sync) {
+// Shared body of the GEMM entry points. ws / counters are used when splits > 1.
+int run_gemm(const void* A, const void* W, void* out, float* resid, const float* bias, int M, int N, int K, int planes,
+             int epi, int out_mode, int act, int bn, const float* cos_t, const float* sin_t, const int* pos,
+             int rope_cols, int geglu_I, void* stream, int sync, int splits, float* ws, int* counters, int* err,
+             int dev) {
   using namespace laya;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
   if ((planes != 1 && planes != 2) || M <= 0 || N <= 0 || K <= 0) return -2;
-  CUtensorMap ta, tb;
-  if (!make_operand_map(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)planes, 128)) return -3;
   if (bn != 128 && bn != 256 && bn != kGemmPair) return -2;
+  CUtensorMap ta, tb, tc;
+  if (!make_operand_map(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)planes, 128)) return -3;
   const uint32_t box_b = bn == kGemmPair ? 128u : static_cast<uint32_t>(bn);  // a pair tile loads 128 B rows per CTA
   if (!make_operand_map(&tb, W, (uint64_t)K, (uint64_t)N, (uint64_t)planes, box_b)) return -3;
-  GemmShape sh{M, N, K, planes == 2 ? 3 : 1};
   const int ncols = epi == EPI_GEGLU ? geglu_I : N;
-  CUtensorMap tc;
   const bool f32 = epi == EPI_RESID || out_mode == OUT_F32;
   void* dst = epi == EPI_RESID ? static_cast<void*>(resid) : out;
   if (!dst || !make_output_map(&tc, dst, f32, (uint64_t)ncols, (uint64_t)M, f32 ? 1 : (out_mode == OUT_BF16X2 ? 2 : 1)))
     return -3;
+  GemmShape sh{M, N, K, planes == 2 ? 3 : 1};
+  sh.splits = splits;
+  sh.ws = ws;
+  sh.counters = counters;
   GemmEpi ep;
   ep.kind = epi;
   ep.out_mode = out_mode;
@@ -57,8 +66,6 @@ extern "C" int laya_b200_gemm(const void* A, const void* W, void* out, float* re
   ep.pos = pos;
   ep.rope_cols = rope_cols;
   ep.geglu_I = geglu_I;
-  int* err = err_word(dev);
-  if (!err) return -4;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = gemm_launch(ta, tb, tc, bn, sh, ep, err, num_sms(dev), st);
   if (e != cudaSuccess) {
@@ -75,4 +82,61 @@ extern "C" int laya_b200_gemm(const void* A, const void* W, void* out, float* re
     }
   }
   return 0;
+}
+}  // namespace
+
+extern "C" int laya_b200_gemm(const void* A, const void* W, void* out, float* resid, const float* bias, int M,
+                              int N, int K, int planes, int epi, int out_mode, int act, int bn,
+                              const float* cos_t, const float* sin_t, const int* pos, int rope_cols,
+                              int geglu_I, void* stream, int sync) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  int* err;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevState* d = dev_state(dev);
+    if (!d) return -4;
+    err = d->err;
+  }
+  return run_gemm(A, W, out, resid, bias, M, N, K, planes, epi, out_mode, act, bn, cos_t, sin_t, pos, rope_cols,
+                  geglu_I, stream, sync, 1, nullptr, nullptr, err, dev);
+}
+
+extern "C" int laya_b200_gemm_splitk(const void* A, const void* W, void* out, float* resid, const float* bias, int M,
+                                     int N, int K, int planes, int epi, int out_mode, int act, int bn,
+                                     const float* cos_t, const float* sin_t, const int* pos, int rope_cols,
+                                     int geglu_I, int splits, void* stream, int sync) {
+  using namespace laya;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  if (splits < 1 || splits > kMaxSplits || (splits > 1 && bn == kGemmPair) || M <= 0 || N <= 0) return -2;
+  float* ws = nullptr;
+  int* counters = nullptr;
+  int* err;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevState* d = dev_state(dev);
+    if (!d) return -4;
+    err = d->err;
+    const size_t need_ws = splitk_ws_floats(M, N, splits), need_ct = splitk_counters(M, N, 128);
+    if (splits > 1 && d->ws_floats < need_ws) {
+      if (d->ws) cudaFree(d->ws);
+      d->ws = nullptr;
+      d->ws_floats = 0;
+      if (cudaMalloc(&d->ws, need_ws * sizeof(float)) != cudaSuccess) return -4;
+      d->ws_floats = need_ws;
+    }
+    if (splits > 1 && d->n_counters < need_ct) {
+      if (d->counters) cudaFree(d->counters);
+      d->counters = nullptr;
+      d->n_counters = 0;
+      if (cudaMalloc(&d->counters, need_ct * sizeof(int)) != cudaSuccess) return -4;
+      if (cudaMemset(d->counters, 0, need_ct * sizeof(int)) != cudaSuccess) return -4;
+      d->n_counters = need_ct;
+    }
+    ws = d->ws;
+    counters = d->counters;
+  }
+  return run_gemm(A, W, out, resid, bias, M, N, K, planes, epi, out_mode, act, bn, cos_t, sin_t, pos, rope_cols,
+                  geglu_I, stream, sync, splits, ws, counters, err, dev);
 }

@@ -117,6 +117,12 @@ class Replica {
   Engine& E;
   const Config& cfg;
   int dev = 0, P = 1, nseg = 1, num_sms = 148, pair_clusters = 0;
+  // split-K workspace (fp32 partials) and its tile counters, sized at load
+  float* ws = nullptr;
+  size_t ws_floats = 0;
+  int* counters = nullptr;
+  size_t n_counters = 0;
+  bool use_splitk = false;
   cudaStream_t st = nullptr;
   std::vector<void*> allocs;
   std::vector<void*> host_allocs;
@@ -368,6 +374,18 @@ class Replica {
     if (!dalloc(&d_logits, (size_t)Rcap * 4, err)) return false;
     if (!dalloc(&d_act, (size_t)Bcap * cfg.n_act * 4, err)) return false;
     if (!dalloc(&d_err, 16, err)) return false;
+    // Split-K (opt-in with LAYA_SPLITK=1): the last slice of each tile sums the workspace partials
+    // of all slices, a chain of L2 round trips that costs more than the idle SMs it recovers on the
+    // shapes measured so far, so the default keeps whole-K tiles. It is chosen only when the
+    // 128 x 128 tiles cannot fill the GPU, i.e. for a few thousand rows at most; 32 M floats
+    // (128 MB) covers every split count there.
+    use_splitk = getenv("LAYA_SPLITK") != nullptr && atoi(getenv("LAYA_SPLITK")) != 0;
+    if (use_splitk) {
+      ws_floats = (size_t)32 << 20;
+      if (!dalloc(&ws, ws_floats * 4, err)) return false;
+      n_counters = splitk_counters(Tcap, std::max(std::max(2 * I, FF), 3 * D), 128);
+      if (!dalloc(&counters, n_counters * 4, err)) return false;
+    }
     const MetaLayout L = meta_layout(Tcap, Bcap, Rcap);
     meta_cap = L.total;
     if (!dalloc(&d_meta, meta_cap * 4, err)) return false;
@@ -490,8 +508,19 @@ class Replica {
     return t256 >= 2LL * num_sms ? 256 : 128;
   }
   void gemm(const Operand& A, int M, const Mat& W, const CUtensorMap& out, const GemmEpi& ep) {
-    const int bn = pick_tile(M, W);
+    int bn = pick_tile(M, W);
     GemmShape sh{M, W.N, W.K, nseg};
+    if (bn == 128 && use_splitk) {
+      // too few 128 x 128 tiles to fill the GPU: split the K loop (deterministic partial sums)
+      const int tiles = ((M + 127) / 128) * ((W.N + 127) / 128);
+      int s = splitk_choose(tiles, ((W.K + 63) / 64) * nseg, num_sms);
+      while (s > 1 && splitk_ws_floats(M, W.N, s) > ws_floats) --s;
+      if (s > 1) {
+        sh.splits = s;
+        sh.ws = ws;
+        sh.counters = counters;
+      }
+    }
     launched(gemm_launch(A.map, bn == 256 ? W.m256 : W.m128, out, bn, sh, ep, d_err, num_sms, st));
   }
   GemmEpi epi_store(int out_mode, const float* bias, int act) const {
@@ -780,6 +809,8 @@ class Replica {
         int zero = 0;
         cudaMemcpy(d_err, &zero, 4, cudaMemcpyHostToDevice);
         *herr = 0;
+        // an aborted split-K launch can leave tile counters part-way: clear them for the next pass
+        if (counters) cudaMemset(counters, 0, n_counters * 4);
       }
       (void)cudaGetLastError();
       return -2;
@@ -969,18 +1000,22 @@ std::vector<std::vector<Question>> Engine::shard(int B, const int* lens, const i
     out[0] = std::move(all);
     return out;
   }
+  std::vector<int> owner(B);
+  shard_owners(B, lens, G, owner.data());
+  for (int b = 0; b < B; ++b) out[owner[b]].push_back(all[b]);
+  return out;
+}
+
+void shard_owners(int B, const int* lens, int G, int* owner) {
   std::vector<int> order(B);
   std::iota(order.begin(), order.end(), 0);
   std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return lens[a] > lens[b]; });
   std::vector<long long> load(G, 0);
-  std::vector<int> owner(B);
   for (int b : order) {
     const int g = (int)(std::min_element(load.begin(), load.end()) - load.begin());
     owner[b] = g;
     load[g] += lens[b] + 64;  // + per-question fixed cost
   }
-  for (int b = 0; b < B; ++b) out[owner[b]].push_back(all[b]);
-  return out;
 }
 
 int Engine::forward_batch(int B, const int* lens, const int* ids, const int* nmark, const int* markers,

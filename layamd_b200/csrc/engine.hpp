@@ -45,6 +45,10 @@ bool plan_passes(int B, const int* lens, const int* nmark, int pass_tokens, int 
 // marker count in [1, 255], every marker inside its sequence.
 bool validate_batch(int B, const int* lens, const int* nmark, const int* markers, int max_len);
 
+// Replica of each question when a call is sharded over G replicas: longest question first onto the
+// least-loaded replica (load = length + 64 per question); ties keep input order.
+void shard_owners(int B, const int* lens, int G, int* owner);
+
 struct Mat {  // a GEMM weight: planes x [N, K] bf16 with its TMA descriptors
   bf16* p = nullptr;
   int N = 0, K = 0;

@@ -136,8 +136,10 @@ __device__ __forceinline__ void emit64(Stager& s, int lane, const CUtensorMap* m
 // Epilogue of one tile for one warp (32 rows starting at row0; thread `lane` holds row row0+lane
 // after each tcgen05.ld). Every tcgen05.ld is executed by the whole warp. Output boxes are clipped by
 // the TMA unit at the row extent of the output map.
-template <int BN, int EPI>
-__device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row0, int lane, int nb, const GemmShape& sh,
+// `ld(off, v)` fills v with tile columns off..off+31 of this thread's row: from tensor memory, or
+// (split-K) summed from the workspace partials.
+template <int BN, int EPI, class Loader>
+__device__ __forceinline__ void epilogue_tile(const Loader& ld, int row0, int lane, int nb, const GemmShape& sh,
                                               const GemmEpi& ep, const CUtensorMap* out_map, Stager& stg) {
   const int row = row0 + lane;
   const bool valid = row < sh.M;
@@ -151,8 +153,8 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row0, int lane
       for (int c = 0; c < 64; c += 32) {
         float xin[32], gate[32];
         __syncwarp();
-        tmem_ld32(tbase + s + c, xin);
-        tmem_ld32(tbase + s + 64 + c, gate);
+        ld(s + c, xin);
+        ld(s + 64 + c, gate);
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[c + i] = gelu_erf(xin[i]) * gate[i];
       }
@@ -179,8 +181,8 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row0, int lane
       if (col >= sh.N) break;
       float v[64];
       __syncwarp();
-      tmem_ld32(tbase + h, *reinterpret_cast<float(*)[32]>(v));
-      tmem_ld32(tbase + h + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+      ld(h, *reinterpret_cast<float(*)[32]>(v));
+      ld(h + 32, *reinterpret_cast<float(*)[32]>(v + 32));
       if (ep.bias) {
 #pragma unroll
         for (int i = 0; i < 64; ++i) v[i] += ep.bias[col + i];
@@ -203,7 +205,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row0, int lane
       if (col >= sh.N) break;
       float v[32];
       __syncwarp();
-      tmem_ld32(tbase + c, v);
+      ld(c, v);
       if (ep.bias) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] += ep.bias[col + i];
@@ -218,8 +220,8 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row0, int lane
       if (col >= sh.N) break;
       float v[64];
       __syncwarp();
-      tmem_ld32(tbase + c, *reinterpret_cast<float(*)[32]>(v));
-      tmem_ld32(tbase + c + 32, *reinterpret_cast<float(*)[32]>(v + 32));  // N is a multiple of 64 here
+      ld(c, *reinterpret_cast<float(*)[32]>(v));
+      ld(c + 32, *reinterpret_cast<float(*)[32]>(v + 32));  // N is a multiple of 64
       if (ep.bias) {
 #pragma unroll
         for (int i = 0; i < 64; ++i) v[i] += ep.bias[col + i];
@@ -233,7 +235,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int row0, int lane
   }
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                    const __grid_constant__ CUtensorMap tc, const GemmShape sh, const GemmEpi ep, int* err) {
@@ -246,7 +248,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_n = (sh.N + BN - 1) / BN;
-  const int tiles = ((sh.M + kBM - 1) / kBM) * num_n;
+  const int splits = SPLIT ? sh.splits : 1;
+  // work unit w = (output tile t, K slice sp), slices of one tile adjacent so they run concurrently
+  const int work = ((sh.M + kBM - 1) / kBM) * num_n * splits;
   const int kb_seg = (sh.K + kBK - 1) / kBK;
   const int nkb = kb_seg * sh.nseg;
 
@@ -270,10 +274,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- TMA producer
       uint32_t stage = 0, phase = 0;
       uint32_t issued_mask = 0, last_phase = 0;  // for the abort drain
-      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      for (int w = blockIdx.x; w < work; w += gridDim.x) {
+        const int t = w / splits, sp = w - t * splits;
         const int mb = t / num_n, nb = t - (t / num_n) * num_n;
+        const int kb0 = sp * nkb / splits, kb1 = (sp + 1) * nkb / splits;
         bool ok = true;
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(smem_u32(&S.empty[stage]), phase ^ 1, abort, err, kErrGemmEmpty)) { ok = false; break; }
           const int seg = kb / kb_seg;
           const int kk = (kb - seg * kb_seg) * kBK;
@@ -305,20 +311,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t stage = 0, phase = 0;
       int local = 0;
       bool issued_any = false;
-      for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
+      for (int w = blockIdx.x; w < work; w += gridDim.x, ++local) {
+        const int sp = w - (w / splits) * splits;
+        const int kb0 = sp * nkb / splits, kb1 = (sp + 1) * nkb / splits;
         const int acc = local & 1;
         const uint32_t accph = (local >> 1) & 1;
         if (!mbar_wait(smem_u32(&S.acce[acc]), accph ^ 1, abort, err, kErrGemmAccEmpty)) break;
         tc_fence_after();
         const uint32_t d = tmem + acc * BN;
         bool ok = true;
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(smem_u32(&S.full[stage]), phase, abort, err, kErrGemmFull)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_u32(S.a[stage]), b0 = smem_u32(S.b[stage]);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)
-            umma_bf16(d, sdesc_k128(a0 + k * 32), sdesc_k128(b0 + k * 32), kIdesc, (kb | k) != 0 ? 1u : 0u);
+            umma_bf16(d, sdesc_k128(a0 + k * 32), sdesc_k128(b0 + k * 32), kIdesc,
+                      (kb != kb0 || k != 0) ? 1u : 0u);
           issued_any = true;
           umma_commit(smem_u32(&S.empty[stage]));
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -340,15 +349,84 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     Stager stager{S.stg[q], 0};
     int local = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
+    for (int w = blockIdx.x; w < work; w += gridDim.x, ++local) {
+      const int t = w / splits, sp = w - t * splits;
       const int acc = local & 1;
       const uint32_t accph = (local >> 1) & 1;
       const int mb = t / num_n, nb = t - (t / num_n) * num_n;
-      const int row = mb * kBM + q * 32 + lane;
+      const int row0 = mb * kBM + q * 32, row = row0 + lane;
       if (!mbar_wait(smem_u32(&S.accf[acc]), accph, abort, err, kErrGemmAccFull)) break;
       tc_fence_after();
       const uint32_t tbase = tmem + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue_tile<BN, EPI>(tbase, mb * kBM + q * 32, lane, nb, sh, ep, &tc, stager);
+      if constexpr (!SPLIT) {
+        epilogue_tile<BN, EPI>([&](int off, float (&v)[32]) { tmem_ld32(tbase + off, v); }, row0, lane, nb, sh, ep,
+                               &tc, stager);
+      } else {
+        // Split-K: publish this slice's fp32 partial rows, then the warp that completes the set of
+        // slices for these 32 rows sums all of them in slice order and runs the epilogue. No CTA
+        // waits for another, and the sum does not depend on which slice finished last.
+        // Both directions go through the warp's swizzled staging tile so that global traffic is
+        // coalesced: lane l moves 16 bytes (float4 l%8) of rows l/8 + 4k.
+        const int cols = min(BN, sh.N - nb * BN);
+        const int f = lane & 7, jr = lane >> 3;
+        const size_t slice = (size_t)sh.M * sh.N;
+        for (int c = 0; c < cols; c += 32) {
+          float v[32];
+          __syncwarp();
+          tmem_ld32(tbase + c, v);
+          uint8_t* tile = stg_acquire(stager, lane);
+          put_f32_row(tile, lane, v);
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int r = 4 * k + jr;
+            if (row0 + r < sh.M)
+              __stcg(reinterpret_cast<float4*>(sh.ws + sp * slice + (size_t)(row0 + r) * sh.N + nb * BN + c) + f,
+                     *reinterpret_cast<const float4*>(tile + r * 128 + ((f ^ (r & 7)) << 4)));
+          }
+        }
+        __syncwarp();
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(sh.counters + (size_t)t * 4 + q, 1) == splits - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();
+          if (lane == 0) sh.counters[(size_t)t * 4 + q] = 0;  // ready for the next launch
+          epilogue_tile<BN, EPI>(
+              [&](int off, float (&v)[32]) {
+                // sum of every slice, 16-byte pieces loaded coalesced (all slices of a piece in
+                // flight together, summed in slice order), then transposed to one row per thread
+                uint8_t* tile = stg_acquire(stager, lane);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                  const int r = 4 * k + jr;
+                  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                  if (row0 + r < sh.M) {
+                    const float4* src =
+                        reinterpret_cast<const float4*>(sh.ws + (size_t)(row0 + r) * sh.N + nb * BN + off) + f;
+                    float4 p[kMaxSplits];
+#pragma unroll
+                    for (int s2 = 0; s2 < kMaxSplits; ++s2)
+                      if (s2 < splits) p[s2] = __ldcg(src + s2 * (slice / 4));
+#pragma unroll
+                    for (int s2 = 0; s2 < kMaxSplits; ++s2)
+                      if (s2 < splits) { acc.x += p[s2].x; acc.y += p[s2].y; acc.z += p[s2].z; acc.w += p[s2].w; }
+                  }
+                  *reinterpret_cast<float4*>(tile + r * 128 + ((f ^ (r & 7)) << 4)) = acc;
+                }
+                __syncwarp();
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const float4 q4 = *reinterpret_cast<const float4*>(tile + lane * 128 + ((j ^ (lane & 7)) << 4));
+                  v[4 * j] = q4.x; v[4 * j + 1] = q4.y; v[4 * j + 2] = q4.z; v[4 * j + 3] = q4.w;
+                }
+                __syncwarp();
+              },
+              row0, lane, nb, sh, ep, &tc, stager);
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&S.acce[acc]));
@@ -357,9 +435,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   tc_fence_before();
+  // Lanes 1..31 of the producer and MMA warps got here while lane 0 ran its loop: reconverge each
+  // warp first, because the block barrier must be reached by whole warps.
+  __syncwarp();
   __syncthreads();
   if (warp == 1) {
-    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 2 * BN);
   }
@@ -501,7 +581,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (!mbar_wait(smem_u32(&S.accf[acc]), accph, abort, err, kErrGemmAccFull)) break;
       tc_fence_after();
       const uint32_t tbase = tmem + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue_tile<BN, EPI>(tbase, row0, lane, nb, sh, ep, &tc, stager);
+      epilogue_tile<BN, EPI>([&](int off, float (&v)[32]) { tmem_ld32(tbase + off, v); }, row0, lane, nb, sh, ep,
+                             &tc, stager);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? acce_leader1 : acce_leader0);
@@ -537,7 +618,10 @@ EncodeTiledFn encode_fn() {
 
 template <int BN, int EPI>
 cudaError_t prepare_one() {
-  return cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)gemm_smem_bytes<BN>());
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               (int)gemm_smem_bytes<BN>());
 }
 
@@ -545,10 +629,11 @@ template <int BN, int EPI>
 cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmShape& sh,
                        const GemmEpi& ep, int* err, int grid_ctas, cudaStream_t st) {
   constexpr size_t smem = gemm_smem_bytes<BN>();
-  const int tiles = ((sh.M + kBM - 1) / kBM) * ((sh.N + BN - 1) / BN);
-  const int grid = tiles < grid_ctas ? tiles : grid_ctas;
+  const int work = ((sh.M + kBM - 1) / kBM) * ((sh.N + BN - 1) / BN) * (sh.splits > 1 ? sh.splits : 1);
+  const int grid = work < grid_ctas ? work : grid_ctas;
   if (grid <= 0) return cudaSuccess;
-  gemm_tc_kernel<BN, EPI><<<grid, kThreads, smem, st>>>(ta, tb, tc, sh, ep, err);
+  if (sh.splits > 1) gemm_tc_kernel<BN, EPI, true><<<grid, kThreads, smem, st>>>(ta, tb, tc, sh, ep, err);
+  else gemm_tc_kernel<BN, EPI, false><<<grid, kThreads, smem, st>>>(ta, tb, tc, sh, ep, err);
   return cudaGetLastError();
 }
 
@@ -651,6 +736,7 @@ cudaError_t gemm_prepare_device() {
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, int bn,
                         const GemmShape& sh, const GemmEpi& ep, int* err, int grid_ctas, cudaStream_t st) {
   if (sh.M <= 0) return cudaSuccess;
+  if (sh.splits > 1 && (bn == kGemmPair || !sh.ws || !sh.counters || sh.splits > kMaxSplits)) return cudaErrorInvalidValue;
   if (sh.N % 64 != 0 || sh.K % 8 != 0 || (sh.nseg != 1 && sh.nseg != 3)) return cudaErrorInvalidValue;
   if (ep.kind == EPI_GEGLU && (ep.geglu_I % 64 != 0 || sh.N != 2 * ep.geglu_I)) return cudaErrorInvalidValue;
   if (ep.kind == EPI_ROPE && (ep.rope_cols % 64 != 0 || !ep.pos || !ep.cos_t || !ep.sin_t))

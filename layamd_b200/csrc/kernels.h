@@ -24,7 +24,35 @@ struct GemmShape {
   int N;     // rows of B, a multiple of 64 (for EPI_GEGLU: 2*I, interleaved as [64 input rows, their 64 gate rows]...)
   int K;     // reduction length of one segment
   int nseg;  // 1 (bf16) or 3 (split-bf16 fp32 emulation)
+  // Split-K (single-CTA tiles only): the K loop is cut into `splits` slices run by different CTAs.
+  // Each slice writes its fp32 partial to ws[splits][M][N]; the last slice to finish sums them in
+  // slice order and runs the epilogue. counters: one int per (128-row tile, 32-row quarter), zero
+  // before the first launch and left zero by every completed launch.
+  int splits = 1;
+  float* ws = nullptr;
+  int* counters = nullptr;
 };
+constexpr int kMaxSplits = 8;
+// Workspace floats and counter ints a split-K launch needs.
+inline size_t splitk_ws_floats(int M, int N, int splits) { return (size_t)splits * M * N; }
+inline size_t splitk_counters(int M, int N, int bn) {
+  return (size_t)((M + 127) / 128) * ((N + bn - 1) / bn) * 4;
+}
+// Slice count that best fills `sms` SMs with `tiles` output tiles and `kblocks` 64-wide K blocks:
+// the smallest S minimising waves(tiles * S) / S, with at least 4 K blocks per slice; 1 when the
+// tiles already fill the GPU.
+inline int splitk_choose(int tiles, int kblocks, int sms) {
+  if (tiles >= sms) return 1;
+  int best = 1;
+  double best_cost = 1e30;
+  for (int s = 1; s <= kMaxSplits; ++s) {
+    if (s > 1 && kblocks / s < 4) break;
+    const int waves = (tiles * s + sms - 1) / sms;
+    const double cost = (double)waves / s * (1.0 + 0.15 * (s - 1));  // each slice adds partial traffic
+    if (cost < best_cost - 1e-9) { best_cost = cost; best = s; }
+  }
+  return best;
+}
 
 // The epilogue writes through the output tensor map `tc` of gemm_launch (make_output_map): bf16
 // planes for OUT_BF16 / OUT_BF16X2 (plane 1 = lo part), fp32 for OUT_F32 and for EPI_RESID, whose

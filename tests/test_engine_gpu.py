@@ -291,6 +291,45 @@ def test_pair_tile_matches_single_cta_tiles(large_ckpt, large_bf16):
     assert act_rel(ac, ac2) < 1e-2
 
 
+def test_splitk_engine_matches_whole_k(large_ckpt, large_bf16):
+    """With LAYA_SPLITK=1 a batch-1 pass (512 rows: too few 128 x 128 tiles to fill the GPU) runs its
+    GEMMs with the K loop split across CTAs; the decisions equal the whole-K ones."""
+    qs = workloads.c2(synth.ARCHS["large"], states=1)
+    rc, lo, ac = large_bf16.forward(qs)
+    assert rc == 0
+    h = Handle(large_ckpt, 0, env={"LAYA_MAX_TOKENS": 4096, "LAYA_SPLITK": 1})
+    try:
+        rc2, lo2, ac2 = h.forward(qs)
+        rc3, lo3, ac3 = h.forward(qs)
+    finally:
+        h.close()
+    assert rc2 == 0 and rc3 == 0
+    assert prob_delta(lo, lo2, qs) < 1e-3
+    assert act_rel(ac, ac2) < 1e-2
+    # slices are summed in a fixed order: a repeated call is bitwise identical
+    assert np.array_equal(lo2, lo3) and np.array_equal(ac2, ac3)
+
+
+def test_multi_device_sharding_matches_one_device(tiny_ckpt):
+    """One handle over several GPUs (LAYA_DEVICES-style device list) shards each call's questions;
+    every question's outputs equal the single-GPU ones."""
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs 2 GPUs")
+    qs = workloads.mixed(synth.ARCHS["tiny"], 50, seed=13, kmax=6)
+    one = Handle(tiny_ckpt, 1, devices="0", env=ENV)
+    many = Handle(tiny_ckpt, 1, devices=",".join(str(i) for i in range(min(n, 4))), env=ENV)
+    try:
+        assert many.L.laya_num_devices(many.h) == min(n, 4)
+        r1 = one.forward(qs)
+        r2 = many.forward(qs)
+        assert r1[0] == 0 and r2[0] == 0
+        assert rel(r2[1], r1[1]) < 1e-5 and rel(r2[2], r1[2]) < 1e-5
+    finally:
+        one.close()
+        many.close()
+
+
 def test_stage_replay_matches_forward(large_bf16):
     from tests.engine_helpers import FP, IP
     qs = workloads.c2(synth.ARCHS["large"], states=8)

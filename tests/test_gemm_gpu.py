@@ -173,3 +173,72 @@ def test_geglu(L, I, bn):
     y = A.double() @ W.double().T
     ref = torch.nn.functional.gelu(y[:, :I]) * y[:, I:]
     assert rel(out, ref) < 1e-4
+
+
+# ---------------------------------------------------------------- split-K (small M)
+@pytest.fixture(scope="module")
+def LS(L):
+    vp, i = ctypes.c_void_p, ctypes.c_int
+    L.laya_b200_gemm_splitk.restype = i
+    L.laya_b200_gemm_splitk.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, i, i, i, i, vp, vp, vp, i, i, i, vp, i]
+    return L
+
+
+def gemm_split(L, splits, A, W, out, M, N, K, planes=1, epi=EPI_STORE, out_mode=OUT_F32, act=0, bn=128, resid=None,
+               bias=None, cos=None, sin=None, pos=None, rope_cols=0, geglu_I=0):
+    torch.cuda.synchronize()
+    rc = L.laya_b200_gemm_splitk(P(A), P(W), P(out), P(resid), P(bias), M, N, K, planes, epi, out_mode, act, bn,
+                                 P(cos), P(sin), P(pos), rope_cols, geglu_I, splits, None, 1)
+    assert rc == 0, "laya_b200_gemm_splitk returned %d" % rc
+
+
+@pytest.mark.parametrize("splits", [2, 3, 4, 8])
+@pytest.mark.parametrize("bn", [128, 256])
+def test_splitk_store_and_resid(LS, splits, bn):
+    M, N, K = 300, 1024, 2624
+    g = torch.Generator(device="cuda").manual_seed(splits)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    W = (0.02 * torch.randn(N, K, device="cuda", generator=g)).bfloat16()
+    b = torch.randn(N, device="cuda", generator=g)
+    ref = A.double() @ W.double().T
+    out = torch.full((M, N), float("nan"), device="cuda")
+    gemm_split(LS, splits, A, W, out, M, N, K, bn=bn)
+    assert rel(out, ref) < 1e-4
+    out2 = torch.full((M, N), float("nan"), device="cuda")
+    gemm_split(LS, splits, A, W, out2, M, N, K, bn=bn)
+    assert torch.equal(out, out2)  # slice sums in fixed order: bitwise repeatable
+    x0 = torch.randn(M, N, device="cuda", generator=g)
+    x = x0.clone()
+    gemm_split(LS, splits, A, W, None, M, N, K, epi=EPI_RESID, resid=x, bias=b, bn=bn)
+    assert rel(x, x0.double() + ref + b.double()) < 1e-5
+
+
+@pytest.mark.parametrize("splits", [2, 4])
+def test_splitk_epilogues(LS, splits):
+    M, K, I = 513, 1024, 1152
+    g = torch.Generator(device="cuda").manual_seed(40 + splits)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    # GeGLU
+    W = (0.03 * torch.randn(2 * I, K, device="cuda", generator=g)).bfloat16()
+    out = torch.empty((M, I), device="cuda")
+    gemm_split(LS, splits, A, interleave_geglu(W, I), out, M, 2 * I, K, epi=EPI_GEGLU, geglu_I=I)
+    y = A.double() @ W.double().T
+    assert rel(out, torch.nn.functional.gelu(y[:, :I]) * y[:, I:]) < 1e-4
+    # RoPE
+    D = 256
+    Wq = (0.05 * torch.randn(3 * D, K, device="cuda", generator=g)).bfloat16()
+    pos = torch.randint(0, 512, (M,), device="cuda", generator=g, dtype=torch.int32)
+    cos, sin = rope_tables(512, 160000.0)
+    outq = torch.empty((M, 3 * D), device="cuda")
+    gemm_split(LS, splits, A, Wq, outq, M, 3 * D, K, epi=EPI_ROPE, cos=cos, sin=sin, pos=pos, rope_cols=2 * D)
+    outq1 = torch.empty((M, 3 * D), device="cuda")
+    gemm(LS, A, Wq, outq1, M, 3 * D, K, epi=EPI_ROPE, cos=cos, sin=sin, pos=pos, rope_cols=2 * D, bn=128)
+    assert rel(outq, outq1) < 1e-5
+    # bias + GELU to bf16 hi/lo planes, fp32-parity operands
+    A32 = torch.randn(M, K, device="cuda", generator=g)
+    W32 = 0.02 * torch.randn(1024, K, device="cuda", generator=g)
+    bb = 0.1 * torch.randn(1024, device="cuda", generator=g)
+    o2 = torch.empty((2, M, 1024), device="cuda", dtype=torch.bfloat16)
+    gemm_split(LS, splits, split(A32), split(W32), o2, M, 1024, K, planes=2, out_mode=OUT_BF16X2, act=2, bias=bb)
+    refg = torch.nn.functional.gelu(A32.double() @ W32.double().T + bb.double())
+    assert rel(o2[0].float() + o2[1].float(), refg) < 1e-4
