@@ -131,6 +131,23 @@ int laya_b200_gemm_splitk(const void* A, const void* W, void* out, float* resid,
                           const float* sin_t, const int* pos, int rope_cols, int geglu_I, int splits, void* stream,
                           int sync);
 
+/* No counterpart in the reference. laya_b200_gemm_splitk for callers that cannot allocate device
+ * memory: a host whose memory manager reserves the GPU's memory up front (a serving stack with a
+ * caching allocator) or a plugin host that forbids allocation in its callbacks, where a cudaMalloc
+ * could fail, fragment the host's pool or stall every stream with its implicit synchronisation. Same
+ * arguments and results; it calls no cudaMalloc or cudaFree. Its scratch is a fixed 16 MiB array in
+ * the library's device image, held by every GPU that loads the library until the process exits:
+ * splits x M x N must stay <= 4194304 fp32 partials and the 128-row tiles x 4 <= 4096 counters,
+ * else the call prints why and returns -7 without launching. The first call on a device sets up
+ * (kernel attributes and the array's device address, no allocation); make it before any stream
+ * capture. Every call on a device shares the array: calls that overlap on the GPU (other streams,
+ * other threads) race and must not be issued. Each call clears the counters and error word it
+ * inherits from the previous one. */
+int laya_b200_gemm_splitk_noalloc(const void* A, const void* W, void* out, float* resid, const float* bias, int M,
+                                  int N, int K, int planes, int epi, int out_mode, int act, int bn,
+                                  const float* cos_t, const float* sin_t, const int* pos, int rope_cols,
+                                  int geglu_I, int splits, void* stream, int sync);
+
 #ifdef __cplusplus
 }
 #endif

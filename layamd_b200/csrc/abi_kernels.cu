@@ -140,3 +140,81 @@ extern "C" int laya_b200_gemm_splitk(const void* A, const void* W, void* out, fl
   return run_gemm(A, W, out, resid, bias, M, N, K, planes, epi, out_mode, act, bn, cos_t, sin_t, pos, rope_cols,
                   geglu_I, stream, sync, splits, ws, counters, err, dev);
 }
+
+// ---------------------------------------------------------------- split-K with no allocation
+// laya_b200_gemm_splitk_noalloc serves callers that may not allocate device memory themselves or
+// let a library do it: a host whose memory manager reserves the GPU's memory up front (a serving
+// stack with a caching allocator, where a cudaMalloc from outside can fail or fragment its pool),
+// or a plugin host that forbids allocation inside its callbacks, where cudaMalloc's implicit device
+// synchronisation would also stall every other stream. Its scratch (split-K partials, tile
+// counters, error word) is this fixed array in the library's device image instead: every GPU that
+// loads the library holds its 16 MiB until the process exits, and every call on a device shares it.
+namespace {
+constexpr size_t kNoAllocWsFloats = size_t(4) << 20;  // fp32 partials: splits x M x N <= 4 Mi (16 MiB)
+constexpr size_t kNoAllocCounters = 4096;              // one per (128-row tile, 32-row quarter)
+constexpr size_t kNoAllocWsBytes = kNoAllocWsFloats * sizeof(float);
+constexpr size_t kNoAllocCtBytes = kNoAllocCounters * sizeof(int);
+constexpr size_t kNoAllocBytes = kNoAllocWsBytes + kNoAllocCtBytes + 256;  // + the error word
+constexpr int kNoAllocMaxDevices = 64;
+}  // namespace
+
+// In host code this name is only a stand-in: its device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_base[kNoAllocMaxDevices];  // device address of g_noalloc_scratch, per device
+
+// Set-up on the first call on a device (with that device current): the kernels' shared-memory
+// limits and the array's device address. Neither allocates.
+unsigned char* noalloc_scratch(int dev) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_base[dev]) {
+    cudaError_t e = laya::gemm_prepare_device();
+    if (e != cudaSuccess) {
+      fprintf(stderr, "[laya] gemm_noalloc: device %d set-up failed: %s\n", dev, cudaGetErrorString(e));
+      return nullptr;
+    }
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      fprintf(stderr, "[laya] gemm_noalloc: no device address for the static scratch on device %d: %s\n", dev,
+              cudaGetErrorString(e));
+      return nullptr;
+    }
+    g_noalloc_base[dev] = static_cast<unsigned char*>(p);
+  }
+  return g_noalloc_base[dev];
+}
+}  // namespace
+
+extern "C" int laya_b200_gemm_splitk_noalloc(const void* A, const void* W, void* out, float* resid, const float* bias,
+                                             int M, int N, int K, int planes, int epi, int out_mode, int act, int bn,
+                                             const float* cos_t, const float* sin_t, const int* pos, int rope_cols,
+                                             int geglu_I, int splits, void* stream, int sync) {
+  using namespace laya;
+  if (splits < 1 || splits > kMaxSplits || (splits > 1 && bn == kGemmPair) || M <= 0 || N <= 0) return -2;
+  const size_t need_ws = splits > 1 ? splitk_ws_floats(M, N, splits) : 0;
+  const size_t need_ct = splits > 1 ? splitk_counters(M, N, 128) : 0;
+  if (need_ws > kNoAllocWsFloats || need_ct > kNoAllocCounters) {
+    fprintf(stderr,
+            "[laya] laya_b200_gemm_splitk_noalloc: M %d x N %d in %d slices needs %zu partial floats and %zu "
+            "counters; the static scratch holds %zu and %zu (use laya_b200_gemm_splitk)\n",
+            M, N, splits, need_ws, need_ct, kNoAllocWsFloats, kNoAllocCounters);
+    return -7;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return -4;
+  unsigned char* base = noalloc_scratch(dev);
+  if (!base) return -4;
+  float* ws = reinterpret_cast<float*>(base);
+  int* counters = reinterpret_cast<int*>(base + kNoAllocWsBytes);
+  int* err = reinterpret_cast<int*>(base + kNoAllocWsBytes + kNoAllocCtBytes);
+  // The array keeps whatever the last call (possibly an aborted one) left: the counters and the
+  // error word, which sit back to back, start every call at zero. The partials need no clearing.
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(counters, 0, kNoAllocCtBytes + sizeof(int), st) != cudaSuccess) return -5;
+  return run_gemm(A, W, out, resid, bias, M, N, K, planes, epi, out_mode, act, bn, cos_t, sin_t, pos, rope_cols,
+                  geglu_I, stream, sync, splits, ws, counters, err, dev);
+}
