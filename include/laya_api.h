@@ -131,6 +131,16 @@ int laya_b200_gemm_splitk(const void* A, const void* W, void* out, float* resid,
                           const float* sin_t, const int* pos, int rope_cols, int geglu_I, int splits, void* stream,
                           int sync);
 
+/* Isolated encoder attention on caller-owned device memory (attention tests and benchmark); replaces
+ * the reference's k_flash_wmma launch (src/kernels.hip:351-356) at kernel level. qkv: bf16
+ * [rows][3 * 64 * H] (q | k | v, heads of 64), sequences packed back to back with lengths lens[B]
+ * (host array, sum <= rows); out: bf16 [rows][64 * H]. window 0: full attention within each
+ * sequence, else |q - k| <= window. impl 0: tcgen05 kernel, 1: mma.sync kernel. Rows of qkv past the
+ * sequences must hold finite values. Uses a library-owned metadata buffer per device: calls must not
+ * overlap on the GPU. Returns 0, -2 bad arguments, -100-code if the kernel reported an error (sync). */
+int laya_b200_attention(const void* qkv, void* out, int rows, int B, const int* lens, int H, int window, int impl,
+                        void* stream, int sync);
+
 /* No counterpart in the reference. laya_b200_gemm_splitk for callers that cannot allocate device
  * memory: a host whose memory manager reserves the GPU's memory up front (a serving stack with a
  * caching allocator) or a plugin host that forbids allocation in its callbacks, where a cudaMalloc

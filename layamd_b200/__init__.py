@@ -61,6 +61,7 @@ def load_lib(path: str = LIB_PATH) -> ctypes.CDLL:
                               ctypes.POINTER(ctypes.c_longlong), i]),
         "laya_b200_gemm": (i, [vp, vp, vp, vp, vp, i, i, i, i, i, i, i, i, vp, vp, vp, i, i, vp, i]),
         "laya_b200_gemm_splitk": (i, [vp, vp, vp, vp, vp, i, i, i, i, i, i, i, i, vp, vp, vp, i, i, i, vp, i]),
+        "laya_b200_attention": (i, [vp, vp, i, i, _IP, i, i, i, vp, i]),
         "laya_b200_gemm_splitk_noalloc": (i, [vp, vp, vp, vp, vp, i, i, i, i, i, i, i, i, vp, vp, vp, i, i, i, vp, i]),
     }
     for name, (res, args) in sig.items():

@@ -1,0 +1,396 @@
+// Encoder attention on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), head dim 64, bf16
+// Q/K/V read in place from the packed qkv rows [T, 3D] (q | k | v, heads of 64), bf16 output rows
+// [T, D]. Replaces the reference's k_flash_wmma (src/kernels.hip:154-242, 351-356) for the encoder
+// layers and the first head layer; the gathered last head layer keeps the mma.sync kernel (attn.cu).
+//
+// Persistent: two CTAs per SM (each 192 threads, 97 KB of shared memory, 256 TMEM columns), each
+// walking its share of the work units (128 query rows of one sequence x one head, the item list
+// sorted longest first) in a software pipeline that runs across unit boundaries:
+//   warp 0      TMA producer: the unit's Q tile into one of two Q slots, then 64-key K and V tiles
+//               into a 4-stage ring (a stage is released when its PV is done), running ahead into
+//               the next units
+//   warp 1      TMEM owner + MMA issuer: S = Q K^T (128 x 64 fp32, two TMEM buffers so S(c+1) is
+//               formed while the softmax of chunk c runs) and O += P V (128 x 64 fp32 in TMEM; P is
+//               the A operand read from tensor memory, V the B operand read MN-major from its TMA
+//               tile)
+//   warps 2..5  softmax, one query row per thread (the row's TMEM lane), one pass over the 64 scores
+//               of a chunk: mask, row max, p = 2^(s*c - m), row sum, P as bf16 pairs into one of two
+//               TMEM buffers. The reference max m is only raised (and O rescaled in TMEM, which waits
+//               for the PV in flight) when it grows by more than 2^8, so chunks normally never wait
+//               for the tensor core; at the end of a unit each thread writes its row of O / l.
+// Keys come only from the unit's own sequence; sliding-window layers visit [q0 - window,
+// q0 + 128 + window). 32-key groups that no row of a warp can see are skipped, groups every row sees
+// completely skip the masking. Masked keys get p = 0 exactly; K / V rows beyond the sequence
+// (another sequence's rows, or zero fill past the buffer) only ever meet p = 0, so they must hold
+// finite values (the engine's qkv buffer starts zeroed).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace laya {
+namespace {
+
+constexpr int kRows = 128;                      // query rows per unit
+constexpr int kKeys = 64;                       // keys per chunk
+constexpr int kStages = 4;                      // K / V ring depth
+constexpr int kThreads = 192;
+constexpr uint32_t kQBytes = 128 * 64 * 2;      // 16 KB
+constexpr uint32_t kKVBytes = 64 * 64 * 2;      // 8 KB
+constexpr uint32_t kTmemCols = 256;             // S buffers at 0 / 64, O at 128, P at 192 / 224 (two CTAs per SM)
+constexpr uint32_t kTmemO = 128;
+constexpr uint32_t kTmemP = 192;                // P bf16 [128 lanes][64 keys] = 32 columns per buffer
+constexpr uint32_t kIdescS = idesc_bf16(128, 64);
+constexpr uint32_t kIdescPV = idesc_bf16(128, 64) | (1u << 16);  // B operand (V) MN-major
+
+struct AttnSmem {
+  alignas(1024) uint8_t q[2][kQBytes];
+  alignas(1024) uint8_t k[kStages][kKVBytes];
+  alignas(1024) uint8_t v[kStages][kKVBytes];
+  alignas(8) uint64_t qfull[2], qempty[2], kfull[kStages], vfull[kStages], kvempty[kStages];
+  uint64_t sfull[2], sfree[2], pfull[2], pfree[2], drain;
+  uint32_t tmem;
+  int abort;
+};
+constexpr size_t attn_smem_bytes() { return sizeof(AttnSmem) + 1024; }
+
+// 2^x on the special-function unit (PTX ex2.approx.ftz.f32; 2^-inf = 0)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Bounded wait for the completion of the last phase issued on a TMA barrier (abort path).
+__device__ __forceinline__ void drain_phase(uint32_t bar, int issued, int* err) {
+  if (issued <= 0) return;
+  const long long t0 = clock64();
+  while (!mbar_try(bar, (issued - 1) & 1)) {
+    if (clock64() - t0 > kWaitBudgetCycles) { atomicCAS(err, 0, kErrGemmDrain); return; }
+  }
+}
+
+// One work unit: 128 query rows [q0, q0+128) of the sequence at packed rows [base, base+len) x head
+// h; keys [lo, lo + 64*nch).
+struct Unit {
+  int base, len, q0, h, lo, nch;
+};
+// Walks this CTA's units (w = blockIdx.x, +gridDim.x, ...) with the next item's 16 bytes already
+// loaded, so no role waits on global memory at a unit boundary. Items hold {seq, q0, base, len};
+// unused slots (seq < 0) sit at the end of the list, so the first one ends the walk.
+struct UnitIter {
+  const AttnArgs& a;
+  int w, nwork;
+  int4 nxt;
+  __device__ __forceinline__ UnitIter(const AttnArgs& args, int n) : a(args), w(blockIdx.x), nwork(n) {
+    nxt = w < nwork ? __ldg(reinterpret_cast<const int4*>(a.items) + w / a.H) : make_int4(-1, 0, 0, 0);
+  }
+  __device__ __forceinline__ bool next(Unit& u) {
+    if (w >= nwork || nxt.x < 0) return false;
+    const int4 it = nxt;
+    u.h = w % a.H;
+    w += gridDim.x;
+    if (w < nwork) nxt = __ldg(reinterpret_cast<const int4*>(a.items) + w / a.H);
+    u.q0 = it.y;
+    u.base = it.z;
+    u.len = it.w;
+    u.lo = a.window > 0 ? max(0, u.q0 - a.window) : 0;
+    const int hi = a.window > 0 ? min(u.len, u.q0 + kRows + a.window) : u.len;
+    u.nch = (hi - u.lo + kKeys - 1) / kKeys;  // >= 1: q0 < len
+    return true;
+  }
+};
+
+__global__ void __launch_bounds__(kThreads, 2)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv, const AttnArgs a,
+                   int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  AttnSmem& S = *reinterpret_cast<AttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int D = a.H * 64;
+  const int nwork = a.n_items * a.H;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&S.qfull[i]), 1);
+      mbar_init(smem_u32(&S.qempty[i]), 1);
+      mbar_init(smem_u32(&S.sfull[i]), 1);
+      mbar_init(smem_u32(&S.sfree[i]), 4);
+      mbar_init(smem_u32(&S.pfull[i]), 4);
+      mbar_init(smem_u32(&S.pfree[i]), 1);
+    }
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(smem_u32(&S.kfull[i]), 1);
+      mbar_init(smem_u32(&S.vfull[i]), 1);
+      mbar_init(smem_u32(&S.kvempty[i]), 1);
+    }
+    mbar_init(smem_u32(&S.drain), 1);
+    S.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tq); tma_prefetch_desc(&tkv); }
+  if (warp == 1) { tmem_alloc(smem_u32(&S.tmem), kTmemCols); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = S.tmem;
+  volatile int* abort = &S.abort;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer. Chunk c uses K / V stage c % kStages (phase c / kStages).
+      int nq[2] = {0, 0}, nk[kStages] = {}, nv[kStages] = {};
+      int c = 0, ui = 0;
+      bool ok = true;
+      UnitIter units(a, nwork);
+      Unit u;
+      while (ok && units.next(u)) {
+        const int qs = ui & 1;
+        if (ui >= 2 && !mbar_wait(smem_u32(&S.qempty[qs]), ((ui >> 1) - 1) & 1, abort, err, kErrAttnLoad)) break;
+        mbar_expect_tx(smem_u32(&S.qfull[qs]), kQBytes);
+        tma_load_3d(smem_u32(S.q[qs]), &tq, u.h * 64, u.base + u.q0, 0, smem_u32(&S.qfull[qs]));
+        ++nq[qs];
+        ++ui;
+        for (int j = 0; j < u.nch; ++j, ++c) {
+          const int st = c % kStages, ph = ((c / kStages) - 1) & 1;
+          const int krow = u.base + u.lo + j * kKeys;
+          if (c >= kStages && !mbar_wait(smem_u32(&S.kvempty[st]), ph, abort, err, kErrAttnLoad)) { ok = false; break; }
+          mbar_expect_tx(smem_u32(&S.kfull[st]), kKVBytes);
+          tma_load_3d(smem_u32(S.k[st]), &tkv, D + u.h * 64, krow, 0, smem_u32(&S.kfull[st]));
+          ++nk[st];
+          mbar_expect_tx(smem_u32(&S.vfull[st]), kKVBytes);
+          tma_load_3d(smem_u32(S.v[st]), &tkv, 2 * D + u.h * 64, krow, 0, smem_u32(&S.vfull[st]));
+          ++nv[st];
+        }
+      }
+      if (*abort) {  // let the loads in flight land before the CTA can exit
+        for (int i = 0; i < 2; ++i) drain_phase(smem_u32(&S.qfull[i]), nq[i], err);
+        for (int i = 0; i < kStages; ++i) {
+          drain_phase(smem_u32(&S.kfull[i]), nk[i], err);
+          drain_phase(smem_u32(&S.vfull[i]), nv[i], err);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer; the PV of chunk c is issued after the S of chunk c+1
+      bool issued = false, ok = true;
+      int c = 0, ui = 0;
+      int pend_c = -1, pend_j = 0;  // chunk whose PV is still to be issued
+      auto issue_pv = [&]() -> bool {
+        const int st = pend_c % kStages, pb = pend_c & 1;
+        if (!mbar_wait(smem_u32(&S.pfull[pb]), (pend_c >> 1) & 1, abort, err, kErrAttnMma)) return false;
+        if (!mbar_wait(smem_u32(&S.vfull[st]), (pend_c / kStages) & 1, abort, err, kErrAttnMma)) return false;
+        tc_fence_after();
+        const uint32_t v_b = smem_u32(S.v[st]);
+#pragma unroll
+        for (int kk = 0; kk < kKeys / 16; ++kk)  // 16 keys = 8 packed TMEM columns of P per step
+          umma_bf16_ts(tmem + kTmemO, tmem + kTmemP + pb * 32 + kk * 8, sdesc_mn128(v_b + kk * 2048), kIdescPV,
+                       (pend_j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(smem_u32(&S.pfree[pb]));
+        umma_commit(smem_u32(&S.kvempty[st]));
+        pend_c = -1;
+        return true;
+      };
+      UnitIter units(a, nwork);
+      Unit u;
+      while (ok && units.next(u)) {
+        const int qs = ui & 1;
+        if (!mbar_wait(smem_u32(&S.qfull[qs]), (ui >> 1) & 1, abort, err, kErrAttnMma)) break;
+        ++ui;
+        const uint32_t q_a = smem_u32(S.q[qs]);
+        for (int j = 0; j < u.nch; ++j, ++c) {
+          const int st = c % kStages, sb = c & 1;
+          if (!mbar_wait(smem_u32(&S.kfull[st]), (c / kStages) & 1, abort, err, kErrAttnMma)) { ok = false; break; }
+          if (c >= 2 && !mbar_wait(smem_u32(&S.sfree[sb]), ((c >> 1) - 1) & 1, abort, err, kErrAttnMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t k_b = smem_u32(S.k[st]);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_bf16(tmem + sb * kKeys, sdesc_k128(q_a + k * 32), sdesc_k128(k_b + k * 32), kIdescS, k > 0 ? 1u : 0u);
+          issued = true;
+          umma_commit(smem_u32(&S.sfull[sb]));
+          if (j == u.nch - 1) umma_commit(smem_u32(&S.qempty[qs]));
+          if (pend_c >= 0 && !issue_pv()) { ok = false; break; }
+          pend_c = c;
+          pend_j = j;
+        }
+      }
+      if (ok && pend_c >= 0) issue_pv();
+      if (*abort && issued) {  // the MMAs already issued finish before TMEM is released
+        umma_commit(smem_u32(&S.drain));
+        const long long t0 = clock64();
+        while (!mbar_try(smem_u32(&S.drain), 0)) {
+          if (clock64() - t0 > kWaitBudgetCycles) { atomicCAS(err, 0, kErrGemmDrain); break; }
+        }
+      }
+    }
+  } else {
+    // ---------------- softmax warps 2..5; warp w owns TMEM lanes (query rows) 32*(w%4) .. +31
+    const int qw = warp & 3;
+    const int row = qw * 32 + lane;
+    const uint32_t tl = tmem + (static_cast<uint32_t>(qw * 32) << 16);
+    const float cs = a.scale * 1.4426950408889634f;  // softmax in base 2
+    const int win = a.window;
+    bf16* out = static_cast<bf16*>(a.out);
+    int c = 0;
+    bool ok = true;
+    UnitIter units(a, nwork);
+    Unit u;
+    while (ok && units.next(u)) {
+      const int qpos = u.q0 + row;
+      const int wr0 = u.q0 + qw * 32;  // first query position of this warp
+      // keys this row can see: [vlo, vlo + span)
+      const int vlo = win > 0 ? max(0, qpos - win) : 0;
+      const int vhi = win > 0 ? min(u.len, qpos + win + 1) : u.len;
+      const unsigned span = vhi > vlo ? static_cast<unsigned>(vhi - vlo) : 0u;
+      float m_used = -INFINITY, lq[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < u.nch; ++j, ++c) {
+        const int k0 = u.lo + j * kKeys, sb = c & 1, pb = c & 1;
+        // per 32-key group, warp-uniform: 0 nobody sees a key, 1 some keys masked, 2 all visible
+        int gk[2];
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const int kg0 = k0 + 32 * g, kg1 = kg0 + 31;
+          if (win == 0) {
+            gk[g] = kg0 >= u.len ? 0 : (kg1 < u.len ? 2 : 1);
+          } else {
+            const bool none = kg0 >= u.len || kg1 < wr0 - win || kg0 > wr0 + 31 + win;
+            const bool all = kg1 < u.len && kg0 >= wr0 + 31 - win && kg1 <= wr0 + win;
+            gk[g] = none ? 0 : (all ? 2 : 1);
+          }
+        }
+        if (!mbar_wait(smem_u32(&S.sfull[sb]), (c >> 1) & 1, abort, err, kErrAttnSoftmax)) { ok = false; break; }
+        tc_fence_after();
+        float t[64];
+        tmem_ld64(tl + sb * kKeys, t);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&S.sfree[sb]));  // the S buffer may take chunk c+2
+        // mask (invisible scores -> -inf) and row max (four independent chains)
+        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          if (gk[g] == 2) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mq[i & 3] = fmaxf(mq[i & 3], t[32 * g + i]);
+          } else if (gk[g] == 1) {
+            const int d0 = k0 + 32 * g - vlo;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              t[32 * g + i] = static_cast<unsigned>(d0 + i) < span ? t[32 * g + i] : -INFINITY;
+              mq[i & 3] = fmaxf(mq[i & 3], t[32 * g + i]);
+            }
+          }
+        }
+        const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * cs;
+        // raise the reference max only when it grows by more than 2^8 (p stays <= 256 otherwise)
+        const float m_new = fmaxf(m_used, mx);
+        const bool resc = m_new > m_used + 8.f;
+        float alpha = 1.f;
+        if (resc) {
+          alpha = ex2(m_used - m_new);  // 0 on the first visible chunk (m_used = -inf)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) lq[k] *= alpha;
+          m_used = m_new;
+        }
+        const float msub = m_used == -INFINITY ? 0.f : m_used;
+        uint32_t pk[32];
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          if (gk[g] == 0) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[16 * g + i] = 0u;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float p0 = ex2(fmaf(t[32 * g + 2 * i], cs, -msub)), p1 = ex2(fmaf(t[32 * g + 2 * i + 1], cs, -msub));
+              lq[(2 * i) & 3] += p0;
+              lq[(2 * i + 1) & 3] += p1;
+              pk[16 * g + i] = pack_bf16x2(p0, p1);
+            }
+          }
+        }
+        // O may only be rescaled once the PV in flight (chunk c-1) has landed
+        if (j > 0 && __any_sync(0xffffffffu, resc)) {
+          if (!mbar_wait(smem_u32(&S.pfree[(c - 1) & 1]), ((c - 1) >> 1) & 1, abort, err, kErrAttnSoftmax)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            float o[32];
+            tmem_ld32(tl + kTmemO + 32 * half, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(tl + kTmemO + 32 * half, o);
+          }
+        }
+        // P buffer pb was last read by the PV of chunk c-2
+        if (c >= 2 && !mbar_wait(smem_u32(&S.pfree[pb]), ((c >> 1) - 1) & 1, abort, err, kErrAttnSoftmax)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        tmem_st32u(tl + kTmemP + pb * 32, pk);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&S.pfull[pb]));
+      }
+      if (!ok) break;
+      // ---- unit epilogue: O / l once the last PV (chunk c-1) has landed
+      const int cl = c - 1;
+      if (!mbar_wait(smem_u32(&S.pfree[cl & 1]), (cl >> 1) & 1, abort, err, kErrAttnSoftmax)) { ok = false; break; }
+      tc_fence_after();
+      const float l = (lq[0] + lq[1]) + (lq[2] + lq[3]);
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      float o[64];
+      tmem_ld64(tl + kTmemO, o);
+      if (row < u.len - u.q0) {
+        uint4* dst = reinterpret_cast<uint4*>(out + (long long)(u.base + qpos) * D + u.h * 64);
+#pragma unroll
+        for (int j8 = 0; j8 < 8; ++j8) {
+          const float* v = o + 8 * j8;
+          dst[j8] = make_uint4(pack_bf16x2(v[0] * inv, v[1] * inv), pack_bf16x2(v[2] * inv, v[3] * inv),
+                               pack_bf16x2(v[4] * inv, v[5] * inv), pack_bf16x2(v[6] * inv, v[7] * inv));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncwarp();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+int g_num_sms = 0;
+
+}  // namespace
+
+cudaError_t attn_tc_prepare_device() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(attn_smem_bytes()));
+}
+
+cudaError_t attn_tc_launch(const CUtensorMap& tq, const CUtensorMap& tkv, const AttnArgs& a, int* err,
+                           cudaStream_t st) {
+  if (a.gathered || a.out_planes != 1 || a.n_items <= 0 || a.H <= 0) return cudaErrorInvalidValue;
+  const int work = a.n_items * a.H;
+  const int sms = g_num_sms > 0 ? g_num_sms : 148;
+  const int grid = work < 2 * sms ? work : 2 * sms;
+  attn_tc_kernel<<<grid, kThreads, attn_smem_bytes(), st>>>(tq, tkv, a, err);
+  return cudaGetLastError();
+}
+
+}  // namespace laya

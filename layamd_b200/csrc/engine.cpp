@@ -48,14 +48,15 @@ size_t align4(size_t n) { return (n + 3) & ~size_t(3); }
 
 // Offsets (in ints) of the per-pass metadata arrays inside the staging block.
 struct MetaLayout {
-  size_t ids, pos, rowseq, soff, slen, qt, nm, moff, items, gitems, gsrc, gdst, grow, total;
-  int items_cap, gitems_cap;
+  size_t ids, pos, rowseq, soff, slen, qt, nm, moff, items, items128, gitems, gsrc, gdst, grow, total;
+  int items_cap, items128_cap, gitems_cap;
 };
 MetaLayout meta_layout(int Tpad, int n, int R) {
   MetaLayout L;
   size_t o = 0;
   auto take = [&](size_t cnt) { size_t r = o; o += align4(cnt); return r; };
   L.items_cap = Tpad / 64 + n;
+  L.items128_cap = Tpad / 128 + n;
   L.gitems_cap = R / 64 + n + 1;
   L.ids = take(Tpad);
   L.pos = take(Tpad);
@@ -66,6 +67,7 @@ MetaLayout meta_layout(int Tpad, int n, int R) {
   L.nm = take(n);
   L.moff = take(n);
   L.items = take((size_t)L.items_cap * 4);
+  L.items128 = take((size_t)L.items128_cap * 4);
   L.gitems = take((size_t)L.gitems_cap * 4);
   L.gsrc = take(R);
   L.gdst = take(R);
@@ -153,6 +155,8 @@ class Replica {
   Operand xn, ao, mg, ff, xng, aog, ffg, xs;
   // epilogue output maps (TMA store / reduce-add targets)
   CUtensorMap out_qkv, out_mg, out_ff, out_ffg, out_x, out_xg, out_hs;
+  CUtensorMap qkv_map, qkv_map64;  // bf16 qkv rows as TMA sources of the tcgen05 attention (Q / K,V boxes)
+  bool attn_tc = false;
   float* xg = nullptr;
   void* hs = nullptr;
   float *d_logits = nullptr, *d_act = nullptr;
@@ -266,6 +270,7 @@ class Replica {
     LAYA_TRY(cudaSetDevice(dev));
     LAYA_TRY(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev));
     LAYA_TRY(gemm_prepare_device());
+    LAYA_TRY(attn_tc_prepare_device());
     pair_clusters = getenv("LAYA_NO_PAIR_GEMM") ? 0 : gemm_pair_clusters();
     LAYA_TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
     P = E.precision == 1 ? 2 : 1;
@@ -357,6 +362,15 @@ class Replica {
     if (!dalloc(&x, (size_t)Tcap * D * 4, err)) return false;
     const size_t qkv_bytes = (size_t)Tcap * 3 * D * (P == 2 ? 4 : 2);
     if (!dalloc(reinterpret_cast<char**>(&qkv), qkv_bytes, err)) return false;
+    // Rows beyond a pass's valid rows are read as masked keys by the tcgen05 attention (p = 0):
+    // they must hold finite values; dalloc zeroes every buffer, and later passes only ever leave
+    // finite GEMM results there.
+    attn_tc = P == 1 && !(getenv("LAYA_ATTN_MMA_SYNC") && atoi(getenv("LAYA_ATTN_MMA_SYNC")) != 0);
+    if (attn_tc && (!make_operand_map(&qkv_map, qkv, 3 * (uint64_t)D, Tcap, 1, 128) ||
+                    !make_operand_map(&qkv_map64, qkv, 3 * (uint64_t)D, Tcap, 1, 64))) {
+      *err = "qkv tensor map rejected";
+      return false;
+    }
     if (!make_operand(&xn, Tcap, D, err) || !make_operand(&ao, Tcap, D, err) || !make_operand(&mg, Tcap, I, err) ||
         !make_operand(&ff, Tcap, FF, err) || !make_operand(&xng, Rcap, D, err) || !make_operand(&aog, Rcap, D, err) ||
         !make_operand(&ffg, Rcap, FF, err) || !make_operand(&xs, Rcap, D, err))
@@ -405,8 +419,9 @@ class Replica {
     const MetaLayout L = meta_layout(p.Tpad, p.n, p.R);
     int* m = h_meta;
     AttnItem* items = reinterpret_cast<AttnItem*>(m + L.items);
+    AttnItem* items128 = reinterpret_cast<AttnItem*>(m + L.items128);
     AttnItem* gitems = reinterpret_cast<AttnItem*>(m + L.gitems);
-    int r = 0, mo = 0, it = 0, git = 0, gl = 0;
+    int r = 0, mo = 0, it = 0, it128 = 0, git = 0, gl = 0;
     for (int i = 0; i < p.n; ++i) {
       const Question& q = qs[p.b0 + i];
       m[L.soff + i] = r;
@@ -420,6 +435,7 @@ class Replica {
         m[L.rowseq + r + j] = i;
       }
       for (int q0 = 0; q0 < q.len; q0 += 64) items[it++] = AttnItem{i, q0, 0, 0};
+      for (int q0 = 0; q0 < q.len; q0 += 128) items128[it128++] = AttnItem{i, q0, r, q.len};  // base row, length
       const int cnt = q.nmark + 1;
       for (int k = 0; k < q.nmark; ++k) {
         m[L.gsrc + gl + k] = r + q.markers[k];
@@ -439,7 +455,10 @@ class Replica {
       m[L.pos + j] = 0;
       m[L.rowseq + j] = -1;
     }
+    // the persistent tcgen05 attention deals its units out round robin: longest sequences first
+    std::stable_sort(items128, items128 + it128, [](const AttnItem& a, const AttnItem& b) { return a.nq > b.nq; });
     for (; it < L.items_cap; ++it) items[it] = AttnItem{-1, 0, 0, 0};
+    for (; it128 < L.items128_cap; ++it128) items128[it128] = AttnItem{-1, 0, 0, 0};
     for (; git < L.gitems_cap; ++git) gitems[git] = AttnItem{-1, 0, 0, 0};
   }
 
@@ -566,6 +585,30 @@ class Replica {
     launched(P == 2 ? attn_f32_launch(a, st) : attn_bf16_launch(a, st));
   }
 
+  // Attention of every packed row into `ao`: the tcgen05 kernel over 128-row items in bf16 mode,
+  // the mma.sync / fp32 kernels over 64-row items otherwise (parity mode, or LAYA_ATTN_MMA_SYNC=1).
+  void attend_rows(const AttnItem* items, int n_items, const AttnItem* items128, int n_items128, const int* soff,
+                   const int* slen, int window) {
+    if (!attn_tc) {
+      attend(items, n_items, soff, slen, window, ao.p, ao.plane, nullptr, nullptr);
+      return;
+    }
+    AttnArgs a;
+    a.qkv = qkv;
+    a.out = ao.p;
+    a.out_plane = ao.plane;
+    a.out_planes = 1;
+    a.items = items128;
+    a.n_items = n_items128;
+    a.soff = soff;
+    a.slen = slen;
+    a.gathered = 0;
+    a.H = cfg.d / 64;
+    a.window = window;
+    a.scale = 0.125f;  // 1/sqrt(64)
+    launched(attn_tc_launch(qkv_map, qkv_map64, a, d_err, st));
+  }
+
   bool dumping() const { return !E.dump_dir.empty() && !capturing && dev == E.reps[0]->dev; }
   void dump(const char* name, const float* src, int rows) {
     if (!dumping()) return;
@@ -589,6 +632,7 @@ class Replica {
               *slen = dm + L.slen, *qt = dm + L.qt, *nm = dm + L.nm, *moff = dm + L.moff, *gsrc = dm + L.gsrc,
               *gdst = dm + L.gdst, *grow = dm + L.grow;
     const AttnItem* items = reinterpret_cast<const AttnItem*>(dm + L.items);
+    const AttnItem* items128 = reinterpret_cast<const AttnItem*>(dm + L.items128);
     const AttnItem* gitems = reinterpret_cast<const AttnItem*>(dm + L.gitems);
     const int qkv_mode = P == 2 ? OUT_F32 : OUT_BF16;
     char nb[32];
@@ -619,7 +663,7 @@ class Replica {
         gemm(xn, M, enc[l].Wqkv, out_qkv, e);
       });
       stage(glob ? "attn_global" : "attn_sliding", [&] {
-        attend(items, L.items_cap, soff, slen, glob ? 0 : cfg.local_attention / 2, ao.p, ao.plane, nullptr, nullptr);
+        attend_rows(items, L.items_cap, items128, L.items128_cap, soff, slen, glob ? 0 : cfg.local_attention / 2);
       });
       stage("gemm_attn_out", [&] { gemm(ao, M, enc[l].Wo, out_x, epi_resid(nullptr)); });
       stage("ln", [&] {
@@ -665,7 +709,7 @@ class Replica {
       const bool last = j == HL - 1;
       stage("head_gemm", [&] { gemm(xn, M, h.inW, out_qkv, epi_store(qkv_mode, h.inB, ACT_NONE)); });
       if (!last) {
-        stage("head_attn", [&] { attend(items, L.items_cap, soff, slen, 0, ao.p, ao.plane, nullptr, nullptr); });
+        stage("head_attn", [&] { attend_rows(items, L.items_cap, items128, L.items128_cap, soff, slen, 0); });
         stage("head_gemm", [&] { gemm(ao, M, h.outW, out_x, epi_resid(h.outB)); });
         stage("head_ln", [&] {
           LnArgs a = ln_base(M);

@@ -93,12 +93,12 @@ cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
                         const GemmShape& sh, const GemmEpi& ep, int* err, int grid_ctas, cudaStream_t st);
 
 // ------------------------------------------------------------------ attention
-// Work item of the attention kernels: 64 query rows of one sequence.
+// Work item of the attention kernels: 64 (mma.sync) or 128 (tcgen05) query rows of one sequence.
 struct AttnItem {
   int seq;   // sequence index within the pass (< 0: unused slot)
   int q0;    // first query position within the sequence (contiguous mode)
-  int goff;  // gathered mode: offset into the gathered-row lists
-  int nq;    // gathered mode: number of query rows (<= 64)
+  int goff;  // gathered mode: offset into the gathered-row lists; tcgen05 items: first packed row
+  int nq;    // gathered mode: number of query rows (<= 64); tcgen05 items: sequence length
 };
 struct AttnArgs {
   const void* qkv;       // [rows, 3*D]: bf16 (fast path) or fp32 (parity path)
@@ -118,6 +118,15 @@ struct AttnArgs {
 };
 cudaError_t attn_bf16_launch(const AttnArgs& a, cudaStream_t st);
 cudaError_t attn_f32_launch(const AttnArgs& a, cudaStream_t st);
+
+// tcgen05 attention (bf16, contiguous mode only): items are 128-query tiles (q0 a multiple of 128;
+// longest sequences first balances the persistent grid), `tq` / `tkv` are make_operand_map over the
+// qkv rows (K = 3*D, rows, 1 plane) with 128-row and 64-row boxes; out is one bf16 plane [rows, D].
+// The K / V rows read past a sequence's end must hold finite values. Bounded waits record an error
+// code in *err. attn_tc_prepare_device() runs once per device first.
+cudaError_t attn_tc_prepare_device();
+cudaError_t attn_tc_launch(const CUtensorMap& tq, const CUtensorMap& tkv, const AttnArgs& a, int* err,
+                           cudaStream_t st);
 
 // ------------------------------------------------------------------ row kernels (LayerNorm family)
 // One warp per row. Source row: emb[ids[r]] (embedding), x[gidx[r]] (gather) or x[r].
