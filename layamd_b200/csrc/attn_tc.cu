@@ -35,8 +35,9 @@ constexpr int kStages = 4;                      // K / V ring depth
 constexpr int kThreads = 192;
 constexpr uint32_t kQBytes = 128 * 64 * 2;      // 16 KB
 constexpr uint32_t kKVBytes = 64 * 64 * 2;      // 8 KB
-constexpr uint32_t kTmemCols = 256;             // S buffers at 0 / 64, O at 128, P at 192 / 224 (two CTAs per SM)
-constexpr uint32_t kTmemO = 128;
+constexpr uint32_t kTmemCols = 256;             // S at 0, O at 64 / 128, P at 192 / 224 (two CTAs per SM)
+constexpr uint32_t kTmemS = 0;
+constexpr uint32_t kTmemO = 64;                 // O of unit parity p at 64 + 64 p
 constexpr uint32_t kTmemP = 192;                // P bf16 [128 lanes][64 keys] = 32 columns per buffer
 constexpr uint32_t kIdescS = idesc_bf16(128, 64);
 constexpr uint32_t kIdescPV = idesc_bf16(128, 64) | (1u << 16);  // B operand (V) MN-major
@@ -46,7 +47,7 @@ struct AttnSmem {
   alignas(1024) uint8_t k[kStages][kKVBytes];
   alignas(1024) uint8_t v[kStages][kKVBytes];
   alignas(8) uint64_t qfull[2], qempty[2], kfull[kStages], vfull[kStages], kvempty[kStages];
-  uint64_t sfull[2], sfree[2], pfull[2], pfree[2], drain;
+  uint64_t sfull, sfree, pfull[2], pfree[2], drain;
   uint32_t tmem;
   int abort;
 };
@@ -57,6 +58,85 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed pairs of fp32 lanes (sm_100 f32x2 FMA pipe): d = a * b + c and d = a + b.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long ra, rb, rc, rd;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(rc) : "f"(c.x), "f"(c.y));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(rd) : "l"(ra), "l"(rb), "l"(rc));
+  float2 d;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  unsigned long long ra, rb, rd;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
+  float2 d;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Asynchronous tensor-memory load / store halves: the matching wait names the registers as
+// operands, so no use of the loaded values (or reuse of the stored ones) is scheduled across it.
+__device__ __forceinline__ void tmem_ld64_issue(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,"
+      "%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,"
+      "%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld64_wait(uint32_t (&r)[64]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31]), "+r"(r[32]), "+r"(r[33]), "+r"(r[34]), "+r"(r[35]),
+                 "+r"(r[36]), "+r"(r[37]), "+r"(r[38]), "+r"(r[39]), "+r"(r[40]), "+r"(r[41]), "+r"(r[42]),
+                 "+r"(r[43]), "+r"(r[44]), "+r"(r[45]), "+r"(r[46]), "+r"(r[47]), "+r"(r[48]), "+r"(r[49]),
+                 "+r"(r[50]), "+r"(r[51]), "+r"(r[52]), "+r"(r[53]), "+r"(r[54]), "+r"(r[55]), "+r"(r[56]),
+                 "+r"(r[57]), "+r"(r[58]), "+r"(r[59]), "+r"(r[60]), "+r"(r[61]), "+r"(r[62]), "+r"(r[63])
+               :
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st32_issue(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+      "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+      "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st32_wait(const uint32_t (&v)[32]) {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::"r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]),
+               "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]),
+               "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]),
+               "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+               "r"(v[29]), "r"(v[30]), "r"(v[31])
+               : "memory");
 }
 
 // Bounded wait for the completion of the last phase issued on a TMA barrier (abort path).
@@ -112,8 +192,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&S.qfull[i]), 1);
       mbar_init(smem_u32(&S.qempty[i]), 1);
-      mbar_init(smem_u32(&S.sfull[i]), 1);
-      mbar_init(smem_u32(&S.sfree[i]), 4);
       mbar_init(smem_u32(&S.pfull[i]), 4);
       mbar_init(smem_u32(&S.pfree[i]), 1);
     }
@@ -122,6 +200,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(smem_u32(&S.vfull[i]), 1);
       mbar_init(smem_u32(&S.kvempty[i]), 1);
     }
+    mbar_init(smem_u32(&S.sfull), 1);
+    mbar_init(smem_u32(&S.sfree), 4);
     mbar_init(smem_u32(&S.drain), 1);
     S.abort = 0;
     fence_mbar_init();
@@ -175,6 +255,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       bool issued = false, ok = true;
       int c = 0, ui = 0;
       int pend_c = -1, pend_j = 0;  // chunk whose PV is still to be issued
+      uint32_t pend_o = kTmemO;     // its O accumulator (per unit parity)
       auto issue_pv = [&]() -> bool {
         const int st = pend_c % kStages, pb = pend_c & 1;
         if (!mbar_wait(smem_u32(&S.pfull[pb]), (pend_c >> 1) & 1, abort, err, kErrAttnMma)) return false;
@@ -183,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t v_b = smem_u32(S.v[st]);
 #pragma unroll
         for (int kk = 0; kk < kKeys / 16; ++kk)  // 16 keys = 8 packed TMEM columns of P per step
-          umma_bf16_ts(tmem + kTmemO, tmem + kTmemP + pb * 32 + kk * 8, sdesc_mn128(v_b + kk * 2048), kIdescPV,
+          umma_bf16_ts(tmem + pend_o, tmem + kTmemP + pb * 32 + kk * 8, sdesc_mn128(v_b + kk * 2048), kIdescPV,
                        (pend_j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(smem_u32(&S.pfree[pb]));
         umma_commit(smem_u32(&S.kvempty[st]));
@@ -198,9 +279,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         ++ui;
         const uint32_t q_a = smem_u32(S.q[qs]);
         for (int j = 0; j < u.nch; ++j, ++c) {
-          const int st = c % kStages, sb = c & 1;
+          const int st = c % kStages;
           if (!mbar_wait(smem_u32(&S.kfull[st]), (c / kStages) & 1, abort, err, kErrAttnMma)) { ok = false; break; }
-          if (c >= 2 && !mbar_wait(smem_u32(&S.sfree[sb]), ((c >> 1) - 1) & 1, abort, err, kErrAttnMma)) {
+          // the softmax has read S(c-1) out of TMEM
+          if (c >= 1 && !mbar_wait(smem_u32(&S.sfree), (c - 1) & 1, abort, err, kErrAttnMma)) {
             ok = false;
             break;
           }
@@ -208,13 +290,14 @@ __global__ void __launch_bounds__(kThreads, 2)
           const uint32_t k_b = smem_u32(S.k[st]);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            umma_bf16(tmem + sb * kKeys, sdesc_k128(q_a + k * 32), sdesc_k128(k_b + k * 32), kIdescS, k > 0 ? 1u : 0u);
+            umma_bf16(tmem + kTmemS, sdesc_k128(q_a + k * 32), sdesc_k128(k_b + k * 32), kIdescS, k > 0 ? 1u : 0u);
           issued = true;
-          umma_commit(smem_u32(&S.sfull[sb]));
+          umma_commit(smem_u32(&S.sfull));
           if (j == u.nch - 1) umma_commit(smem_u32(&S.qempty[qs]));
           if (pend_c >= 0 && !issue_pv()) { ok = false; break; }
           pend_c = c;
           pend_j = j;
+          pend_o = kTmemO + static_cast<uint32_t>(((ui - 1) & 1) * 64);
         }
       }
       if (ok && pend_c >= 0) issue_pv();
@@ -234,20 +317,58 @@ __global__ void __launch_bounds__(kThreads, 2)
     const float cs = a.scale * 1.4426950408889634f;  // softmax in base 2
     const int win = a.window;
     bf16* out = static_cast<bf16*>(a.out);
-    int c = 0;
+    int c = 0, uiu = 0;
     bool ok = true;
+    // The epilogue of a unit (O / l out of TMEM into the output rows) runs after the first chunk of
+    // the next unit, when the unit's last PV has long finished; O is double-buffered per unit parity.
+    struct Pending {
+      bool on;
+      int cl;          // last chunk of the unit
+      uint32_t oc;     // its O columns
+      long long row0;  // output row of this thread (packed)
+      int h;
+      bool valid;      // this thread's query row lies inside the sequence
+      float inv;       // 1 / l
+    } pe{false, 0, 0, 0, 0, false, 0.f};
+    auto flush = [&]() -> bool {
+      if (!pe.on) return true;
+      pe.on = false;
+      if (!mbar_wait(smem_u32(&S.pfree[pe.cl & 1]), (pe.cl >> 1) & 1, abort, err, kErrAttnSoftmax)) return false;
+      tc_fence_after();
+      uint4* dst = reinterpret_cast<uint4*>(out + pe.row0 * D + pe.h * 64);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float o[32];
+        tmem_ld32(tl + pe.oc + 32 * half, o);
+        if (pe.valid) {
+#pragma unroll
+          for (int j8 = 0; j8 < 4; ++j8) {
+            const float* v = o + 8 * j8;
+            const float inv = pe.inv;
+            dst[4 * half + j8] = make_uint4(pack_bf16x2(v[0] * inv, v[1] * inv), pack_bf16x2(v[2] * inv, v[3] * inv),
+                                            pack_bf16x2(v[4] * inv, v[5] * inv), pack_bf16x2(v[6] * inv, v[7] * inv));
+          }
+        }
+      }
+      tc_fence_before();  // O is rewritten by the unit after next only after this warp's later arrivals
+      return true;
+    };
     UnitIter units(a, nwork);
     Unit u;
-    while (ok && units.next(u)) {
+    bool have = units.next(u);
+    while (ok && have) {
+      const uint32_t oc = kTmemO + static_cast<uint32_t>((uiu & 1) * 64);
+      ++uiu;
       const int qpos = u.q0 + row;
       const int wr0 = u.q0 + qw * 32;  // first query position of this warp
       // keys this row can see: [vlo, vlo + span)
       const int vlo = win > 0 ? max(0, qpos - win) : 0;
       const int vhi = win > 0 ? min(u.len, qpos + win + 1) : u.len;
       const unsigned span = vhi > vlo ? static_cast<unsigned>(vhi - vlo) : 0u;
-      float m_used = -INFINITY, lq[4] = {0.f, 0.f, 0.f, 0.f};
+      float m_used = -INFINITY;
+      float2 la = make_float2(0.f, 0.f), lb = make_float2(0.f, 0.f);
       for (int j = 0; j < u.nch; ++j, ++c) {
-        const int k0 = u.lo + j * kKeys, sb = c & 1, pb = c & 1;
+        const int k0 = u.lo + j * kKeys, pb = c & 1;
         // per 32-key group, warp-uniform: 0 nobody sees a key, 1 some keys masked, 2 all visible
         int gk[2];
 #pragma unroll
@@ -261,41 +382,42 @@ __global__ void __launch_bounds__(kThreads, 2)
             gk[g] = none ? 0 : (all ? 2 : 1);
           }
         }
-        if (!mbar_wait(smem_u32(&S.sfull[sb]), (c >> 1) & 1, abort, err, kErrAttnSoftmax)) { ok = false; break; }
+        // mask (invisible scores -> -inf) and row max (three-input max, four chains)
+        if (!mbar_wait(smem_u32(&S.sfull), c & 1, abort, err, kErrAttnSoftmax)) { ok = false; break; }
         tc_fence_after();
-        float t[64];
-        tmem_ld64(tl + sb * kKeys, t);
+        uint32_t tr[64];
+        tmem_ld64_issue(tl + kTmemS, tr);
+        tmem_ld64_wait(tr);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&S.sfree[sb]));  // the S buffer may take chunk c+2
-        // mask (invisible scores -> -inf) and row max (four independent chains)
+        if (lane == 0) mbar_arrive(smem_u32(&S.sfree));  // S may take chunk c+1
         float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
-          if (gk[g] == 2) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) mq[i & 3] = fmaxf(mq[i & 3], t[32 * g + i]);
-          } else if (gk[g] == 1) {
+          if (gk[g] == 1) {
             const int d0 = k0 + 32 * g - vlo;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              t[32 * g + i] = static_cast<unsigned>(d0 + i) < span ? t[32 * g + i] : -INFINITY;
-              mq[i & 3] = fmaxf(mq[i & 3], t[32 * g + i]);
-            }
+            for (int i = 0; i < 32; ++i)
+              if (static_cast<unsigned>(d0 + i) >= span) tr[32 * g + i] = 0xff800000u;  // -inf
+          }
+          if (gk[g] != 0) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 2)
+              mq[(i >> 1) & 3] = fmax3(mq[(i >> 1) & 3], __uint_as_float(tr[32 * g + i]), __uint_as_float(tr[32 * g + i + 1]));
           }
         }
-        const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * cs;
+        const float mx = fmax3(mq[0], mq[1], fmaxf(mq[2], mq[3])) * cs;
         // raise the reference max only when it grows by more than 2^8 (p stays <= 256 otherwise)
         const float m_new = fmaxf(m_used, mx);
         const bool resc = m_new > m_used + 8.f;
         float alpha = 1.f;
         if (resc) {
           alpha = ex2(m_used - m_new);  // 0 on the first visible chunk (m_used = -inf)
-#pragma unroll
-          for (int k = 0; k < 4; ++k) lq[k] *= alpha;
+          la.x *= alpha; la.y *= alpha; lb.x *= alpha; lb.y *= alpha;
           m_used = m_new;
         }
         const float msub = m_used == -INFINITY ? 0.f : m_used;
+        const float2 cs2 = make_float2(cs, cs), nm2 = make_float2(-msub, -msub);
         uint32_t pk[32];
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
@@ -305,10 +427,11 @@ __global__ void __launch_bounds__(kThreads, 2)
           } else {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const float p0 = ex2(fmaf(t[32 * g + 2 * i], cs, -msub)), p1 = ex2(fmaf(t[32 * g + 2 * i + 1], cs, -msub));
-              lq[(2 * i) & 3] += p0;
-              lq[(2 * i + 1) & 3] += p1;
-              pk[16 * g + i] = pack_bf16x2(p0, p1);
+              const float2 x =
+                  ffma2(make_float2(__uint_as_float(tr[32 * g + 2 * i]), __uint_as_float(tr[32 * g + 2 * i + 1])), cs2, nm2);
+              const float2 pp = make_float2(ex2(x.x), ex2(x.y));
+              if (i & 1) lb = fadd2(lb, pp); else la = fadd2(la, pp);
+              pk[16 * g + i] = pack_bf16x2(pp.x, pp.y);
             }
           }
         }
@@ -322,10 +445,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             float o[32];
-            tmem_ld32(tl + kTmemO + 32 * half, o);
+            tmem_ld32(tl + oc + 32 * half, o);
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(tl + kTmemO + 32 * half, o);
+            tmem_st32(tl + oc + 32 * half, o);
           }
         }
         // P buffer pb was last read by the PV of chunk c-2
@@ -334,30 +457,26 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         }
         tc_fence_after();
-        tmem_st32u(tl + kTmemP + pb * 32, pk);
+        tmem_st32_issue(tl + kTmemP + pb * 32, pk);
+        tmem_st32_wait(pk);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&S.pfull[pb]));
+        if (j == 0 && !flush()) { ok = false; break; }
       }
       if (!ok) break;
-      // ---- unit epilogue: O / l once the last PV (chunk c-1) has landed
-      const int cl = c - 1;
-      if (!mbar_wait(smem_u32(&S.pfree[cl & 1]), (cl >> 1) & 1, abort, err, kErrAttnSoftmax)) { ok = false; break; }
-      tc_fence_after();
-      const float l = (lq[0] + lq[1]) + (lq[2] + lq[3]);
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      float o[64];
-      tmem_ld64(tl + kTmemO, o);
-      if (row < u.len - u.q0) {
-        uint4* dst = reinterpret_cast<uint4*>(out + (long long)(u.base + qpos) * D + u.h * 64);
-#pragma unroll
-        for (int j8 = 0; j8 < 8; ++j8) {
-          const float* v = o + 8 * j8;
-          dst[j8] = make_uint4(pack_bf16x2(v[0] * inv, v[1] * inv), pack_bf16x2(v[2] * inv, v[3] * inv),
-                               pack_bf16x2(v[4] * inv, v[5] * inv), pack_bf16x2(v[6] * inv, v[7] * inv));
-        }
-      }
+      // ---- this unit's epilogue, deferred until after the next unit's first chunk
+      const float l = (la.x + la.y) + (lb.x + lb.y);
+      pe.on = true;
+      pe.cl = c - 1;
+      pe.oc = oc;
+      pe.row0 = (long long)u.base + qpos;
+      pe.h = u.h;
+      pe.valid = row < u.len - u.q0;
+      pe.inv = l > 0.f ? 1.f / l : 0.f;
+      have = units.next(u);
     }
+    if (ok && !flush()) ok = false;
   }
 
   tc_fence_before();
