@@ -1,6 +1,7 @@
 // Kernel-level C entry point for the encoder attention on caller-owned device buffers: the attention
 // parity tests and the isolated attention benchmark use it. An addition to the reference ABI; the
 // engine itself never calls it.
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 #include <vector>
@@ -13,6 +14,7 @@ std::mutex g_mu;
 struct AttnDev {
   bool ready = false;
   int* err = nullptr;      // device error word
+  int* ticket = nullptr;   // work counter of the persistent tcgen05 kernel
   int* meta = nullptr;     // soff[B] | slen[B] | items (4 ints each)
   size_t meta_ints = 0;
 };
@@ -41,10 +43,13 @@ extern "C" int laya_b200_attention(const void* qkv, void* out, int rows, int B, 
     for (int q0 = 0; q0 < lens[i]; q0 += qrows) items.push_back(AttnItem{i, q0, off, lens[i]});
     off += lens[i];
   }
+  if (impl == 0)  // the tcgen05 kernel hands units out longest sequence first, as the engine orders them
+    std::stable_sort(items.begin(), items.end(), [](const AttnItem& x, const AttnItem& y) { return x.nq > y.nq; });
   const size_t n_ints = meta.size() + items.size() * 4;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int* d_meta;
   int* err;
+  int* ticket;
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if ((int)g_dev.size() <= dev) g_dev.resize(dev + 1);
@@ -52,6 +57,7 @@ extern "C" int laya_b200_attention(const void* qkv, void* out, int rows, int B, 
     if (!d.ready) {
       if (attn_tc_prepare_device() != cudaSuccess) return -4;
       if (cudaMalloc(&d.err, sizeof(int)) != cudaSuccess) return -4;
+      if (cudaMalloc(&d.ticket, sizeof(int)) != cudaSuccess) return -4;
       if (cudaMemset(d.err, 0, sizeof(int)) != cudaSuccess) return -4;
       d.ready = true;
     }
@@ -64,6 +70,7 @@ extern "C" int laya_b200_attention(const void* qkv, void* out, int rows, int B, 
     }
     d_meta = d.meta;
     err = d.err;
+    ticket = d.ticket;
   }
   // the previous call may still read the metadata block: order the upload after it on the stream
   if (cudaMemcpyAsync(d_meta, meta.data(), meta.size() * sizeof(int), cudaMemcpyHostToDevice, st) != cudaSuccess ||
@@ -92,7 +99,7 @@ extern "C" int laya_b200_attention(const void* qkv, void* out, int rows, int B, 
     if (!make_operand_map(&tq, qkv, 3ull * 64 * H, (uint64_t)rows, 1, 128) ||
         !make_operand_map(&tkv, qkv, 3ull * 64 * H, (uint64_t)rows, 1, 64))
       return -3;
-    e = attn_tc_launch(tq, tkv, a, err, st);
+    e = attn_tc_launch(tq, tkv, a, ticket, err, st);
   } else {
     e = attn_bf16_launch(a, st);
   }

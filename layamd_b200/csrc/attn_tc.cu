@@ -3,10 +3,12 @@
 // [T, D]. Replaces the reference's k_flash_wmma (src/kernels.hip:154-242, 351-356) for the encoder
 // layers and the first head layer; the gathered last head layer keeps the mma.sync kernel (attn.cu).
 //
-// Persistent: two CTAs per SM (each 192 threads, 97 KB of shared memory, 256 TMEM columns), each
-// walking its share of the work units (128 query rows of one sequence x one head, the item list
-// sorted longest first) in a software pipeline that runs across unit boundaries:
-//   warp 0      TMA producer: the unit's Q tile into one of two Q slots, then 64-key K and V tiles
+// Persistent: two CTAs per SM (each 192 threads, 97 KB of shared memory, 256 TMEM columns). Work
+// units (128 query rows of one sequence x one head, the item list sorted longest first) are claimed
+// dynamically from a global counter, so the longest remaining unit always goes to the next free CTA,
+// and each CTA runs its units through a software pipeline that continues across unit boundaries:
+//   warp 0      TMA producer: claims units and publishes them to the other roles through a 4-deep
+//               ring in shared memory; the unit's Q tile into one of two Q slots, then 64-key K and V tiles
 //               into a 4-stage ring (a stage is released when its PV is done), running ahead into
 //               the next units
 //   warp 1      TMEM owner + MMA issuer: S = Q K^T (128 x 64 fp32, two TMEM buffers so S(c+1) is
@@ -33,6 +35,7 @@ constexpr int kRows = 128;                      // query rows per unit
 constexpr int kKeys = 64;                       // keys per chunk
 constexpr int kStages = 4;                      // K / V ring depth
 constexpr int kThreads = 192;
+constexpr int kRing = 4;                        // claimed units published ahead to the MMA / softmax roles
 constexpr uint32_t kQBytes = 128 * 64 * 2;      // 16 KB
 constexpr uint32_t kKVBytes = 64 * 64 * 2;      // 8 KB
 constexpr uint32_t kTmemCols = 256;             // S at 0, O at 64 / 128, P at 192 / 224 (two CTAs per SM)
@@ -42,11 +45,19 @@ constexpr uint32_t kTmemP = 192;                // P bf16 [128 lanes][64 keys] =
 constexpr uint32_t kIdescS = idesc_bf16(128, 64);
 constexpr uint32_t kIdescPV = idesc_bf16(128, 64) | (1u << 16);  // B operand (V) MN-major
 
+// One work unit: 128 query rows [q0, q0+128) of the sequence at packed rows [base, base+len) x head
+// h; keys [lo, lo + 64*nch). nch == 0 marks the end of the work.
+struct Unit {
+  int base, len, q0, h, lo, nch;
+};
+
 struct AttnSmem {
   alignas(1024) uint8_t q[2][kQBytes];
   alignas(1024) uint8_t k[kStages][kKVBytes];
   alignas(1024) uint8_t v[kStages][kKVBytes];
-  alignas(8) uint64_t qfull[2], qempty[2], kfull[kStages], vfull[kStages], kvempty[kStages];
+  Unit units[kRing];
+  alignas(8) uint64_t ufull[kRing], uempty[kRing];
+  uint64_t qfull[2], qempty[2], kfull[kStages], vfull[kStages], kvempty[kStages];
   uint64_t sfull, sfree, pfull[2], pfree[2], drain;
   uint32_t tmem;
   int abort;
@@ -148,40 +159,36 @@ __device__ __forceinline__ void drain_phase(uint32_t bar, int issued, int* err) 
   }
 }
 
-// One work unit: 128 query rows [q0, q0+128) of the sequence at packed rows [base, base+len) x head
-// h; keys [lo, lo + 64*nch).
-struct Unit {
-  int base, len, q0, h, lo, nch;
-};
-// Walks this CTA's units (w = blockIdx.x, +gridDim.x, ...) with the next item's 16 bytes already
-// loaded, so no role waits on global memory at a unit boundary. Items hold {seq, q0, base, len};
-// unused slots (seq < 0) sit at the end of the list, so the first one ends the walk.
-struct UnitIter {
-  const AttnArgs& a;
-  int w, nwork;
-  int4 nxt;
-  __device__ __forceinline__ UnitIter(const AttnArgs& args, int n) : a(args), w(blockIdx.x), nwork(n) {
-    nxt = w < nwork ? __ldg(reinterpret_cast<const int4*>(a.items) + w / a.H) : make_int4(-1, 0, 0, 0);
-  }
-  __device__ __forceinline__ bool next(Unit& u) {
-    if (w >= nwork || nxt.x < 0) return false;
-    const int4 it = nxt;
-    u.h = w % a.H;
-    w += gridDim.x;
-    if (w < nwork) nxt = __ldg(reinterpret_cast<const int4*>(a.items) + w / a.H);
-    u.q0 = it.y;
-    u.base = it.z;
-    u.len = it.w;
-    u.lo = a.window > 0 ? max(0, u.q0 - a.window) : 0;
-    const int hi = a.window > 0 ? min(u.len, u.q0 + kRows + a.window) : u.len;
-    u.nch = (hi - u.lo + kKeys - 1) / kKeys;  // >= 1: q0 < len
-    return true;
-  }
-};
+// Unit w of the launch (item w / H, head w % H); false past the last one. Items hold
+// {seq, q0, base, len}, longest sequences first; unused slots (seq < 0) sit at the end.
+__device__ __forceinline__ bool unit_of(const AttnArgs& a, int w, int nwork, Unit& u) {
+  if (w >= nwork) return false;
+  const int4 it = __ldg(reinterpret_cast<const int4*>(a.items) + w / a.H);
+  if (it.x < 0) return false;
+  u.h = w % a.H;
+  u.q0 = it.y;
+  u.base = it.z;
+  u.len = it.w;
+  u.lo = a.window > 0 ? max(0, u.q0 - a.window) : 0;
+  const int hi = a.window > 0 ? min(u.len, u.q0 + kRows + a.window) : u.len;
+  u.nch = (hi - u.lo + kKeys - 1) / kKeys;  // >= 1: q0 < len
+  return true;
+}
+
+// Consumer side of the unit ring: the `ui`-th unit this CTA claimed (all lanes of a warp call it).
+__device__ __forceinline__ bool take_unit(AttnSmem& S, int ui, Unit& u, volatile int* abort, int* err, int code,
+                                          int lane) {
+  const int rs = ui % kRing;
+  if (!mbar_wait(smem_u32(&S.ufull[rs]), (ui / kRing) & 1, abort, err, code)) return false;
+  u = S.units[rs];
+  __syncwarp(__activemask());
+  if (lane == 0) mbar_arrive(smem_u32(&S.uempty[rs]));
+  return u.nch > 0;
+}
 
 __global__ void __launch_bounds__(kThreads, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv, const AttnArgs a,
-                   int* err) {
+                   int* ticket, int* err) {
   extern __shared__ uint8_t smem_raw[];
   AttnSmem& S = *reinterpret_cast<AttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -199,6 +206,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(smem_u32(&S.kfull[i]), 1);
       mbar_init(smem_u32(&S.vfull[i]), 1);
       mbar_init(smem_u32(&S.kvempty[i]), 1);
+    }
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(smem_u32(&S.ufull[i]), 1);
+      mbar_init(smem_u32(&S.uempty[i]), 5);  // the MMA issuer and the four softmax warps
     }
     mbar_init(smem_u32(&S.sfull), 1);
     mbar_init(smem_u32(&S.sfree), 4);
@@ -218,11 +229,19 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       // ---------------- TMA producer. Chunk c uses K / V stage c % kStages (phase c / kStages).
       int nq[2] = {0, 0}, nk[kStages] = {}, nv[kStages] = {};
-      int c = 0, ui = 0;
+      int c = 0, ui = 0, nu = 0;
       bool ok = true;
-      UnitIter units(a, nwork);
-      Unit u;
-      while (ok && units.next(u)) {
+      while (ok) {
+        // claim the next unit (dynamic: the longest remaining first) and publish it
+        const int rs = nu % kRing;
+        if (nu >= kRing && !mbar_wait(smem_u32(&S.uempty[rs]), ((nu / kRing) - 1) & 1, abort, err, kErrAttnLoad)) break;
+        Unit u;
+        const bool valid = unit_of(a, atomicAdd(ticket, 1), nwork, u);
+        if (!valid) u.nch = 0;
+        S.units[rs] = u;
+        mbar_arrive(smem_u32(&S.ufull[rs]));
+        ++nu;
+        if (!valid) break;
         const int qs = ui & 1;
         if (ui >= 2 && !mbar_wait(smem_u32(&S.qempty[qs]), ((ui >> 1) - 1) & 1, abort, err, kErrAttnLoad)) break;
         mbar_expect_tx(smem_u32(&S.qfull[qs]), kQBytes);
@@ -271,9 +290,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         pend_c = -1;
         return true;
       };
-      UnitIter units(a, nwork);
       Unit u;
-      while (ok && units.next(u)) {
+      for (int nu = 0; ok && take_unit(S, nu, u, abort, err, kErrAttnMma, 0); ++nu) {
         const int qs = ui & 1;
         if (!mbar_wait(smem_u32(&S.qfull[qs]), (ui >> 1) & 1, abort, err, kErrAttnMma)) break;
         ++ui;
@@ -353,9 +371,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_fence_before();  // O is rewritten by the unit after next only after this warp's later arrivals
       return true;
     };
-    UnitIter units(a, nwork);
     Unit u;
-    bool have = units.next(u);
+    int nu = 0;
+    bool have = take_unit(S, nu++, u, abort, err, kErrAttnSoftmax, lane);
     while (ok && have) {
       const uint32_t oc = kTmemO + static_cast<uint32_t>((uiu & 1) * 64);
       ++uiu;
@@ -474,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       pe.h = u.h;
       pe.valid = row < u.len - u.q0;
       pe.inv = l > 0.f ? 1.f / l : 0.f;
-      have = units.next(u);
+      have = take_unit(S, nu++, u, abort, err, kErrAttnSoftmax, lane);
     }
     if (ok && !flush()) ok = false;
   }
@@ -502,13 +520,15 @@ cudaError_t attn_tc_prepare_device() {
                               static_cast<int>(attn_smem_bytes()));
 }
 
-cudaError_t attn_tc_launch(const CUtensorMap& tq, const CUtensorMap& tkv, const AttnArgs& a, int* err,
+cudaError_t attn_tc_launch(const CUtensorMap& tq, const CUtensorMap& tkv, const AttnArgs& a, int* ticket, int* err,
                            cudaStream_t st) {
-  if (a.gathered || a.out_planes != 1 || a.n_items <= 0 || a.H <= 0) return cudaErrorInvalidValue;
+  if (a.gathered || a.out_planes != 1 || a.n_items <= 0 || a.H <= 0 || !ticket) return cudaErrorInvalidValue;
+  cudaError_t e = cudaMemsetAsync(ticket, 0, sizeof(int), st);  // the work counter starts at zero
+  if (e != cudaSuccess) return e;
   const int work = a.n_items * a.H;
   const int sms = g_num_sms > 0 ? g_num_sms : 148;
   const int grid = work < 2 * sms ? work : 2 * sms;
-  attn_tc_kernel<<<grid, kThreads, attn_smem_bytes(), st>>>(tq, tkv, a, err);
+  attn_tc_kernel<<<grid, kThreads, attn_smem_bytes(), st>>>(tq, tkv, a, ticket, err);
   return cudaGetLastError();
 }
 

@@ -157,6 +157,7 @@ class Replica {
   CUtensorMap out_qkv, out_mg, out_ff, out_ffg, out_x, out_xg, out_hs;
   CUtensorMap qkv_map, qkv_map64;  // bf16 qkv rows as TMA sources of the tcgen05 attention (Q / K,V boxes)
   bool attn_tc = false;
+  int* d_attn_ticket = nullptr;  // work counter of the persistent attention kernel
   float* xg = nullptr;
   void* hs = nullptr;
   float *d_logits = nullptr, *d_act = nullptr;
@@ -388,6 +389,7 @@ class Replica {
     if (!dalloc(&d_logits, (size_t)Rcap * 4, err)) return false;
     if (!dalloc(&d_act, (size_t)Bcap * cfg.n_act * 4, err)) return false;
     if (!dalloc(&d_err, 16, err)) return false;
+    if (!dalloc(&d_attn_ticket, 16, err)) return false;
     // Split-K (opt-in with LAYA_SPLITK=1): the last slice of each tile sums the workspace partials
     // of all slices, a chain of L2 round trips that costs more than the idle SMs it recovers on the
     // shapes measured so far, so the default keeps whole-K tiles. It is chosen only when the
@@ -606,7 +608,7 @@ class Replica {
     a.H = cfg.d / 64;
     a.window = window;
     a.scale = 0.125f;  // 1/sqrt(64)
-    launched(attn_tc_launch(qkv_map, qkv_map64, a, d_err, st));
+    launched(attn_tc_launch(qkv_map, qkv_map64, a, d_attn_ticket, d_err, st));
   }
 
   bool dumping() const { return !E.dump_dir.empty() && !capturing && dev == E.reps[0]->dev; }

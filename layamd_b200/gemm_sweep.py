@@ -33,9 +33,10 @@ def peaks():
 
 
 def pick_tile(M, N, sms):
-    """The engine's rule (engine.cpp pick_bn) for the single-CTA tiles."""
-    if N < 256:
-        return 128
+    """The engine's rule (engine.cpp Replica::pick_tile): the CTA-pair 256 x 256 tile when its tiles
+    fill every co-resident pair twice, else 128 x 256 when those fill every SM twice, else 128 x 128."""
+    if ((M + 255) // 256) * ((N + 255) // 256) >= 2 * (sms // 2):
+        return 512
     return 256 if ((M + 127) // 128) * ((N + 255) // 256) >= 2 * sms else 128
 
 
