@@ -14,7 +14,7 @@ std::mutex g_mu;
 struct AttnDev {
   bool ready = false;
   int* err = nullptr;      // device error word
-  int* ticket = nullptr;   // work counter of the persistent tcgen05 kernel
+  int* ticket = nullptr;   // work / exit counters of the persistent tcgen05 kernel (kept zero between launches)
   int* meta = nullptr;     // soff[B] | slen[B] | items (4 ints each)
   size_t meta_ints = 0;
 };
@@ -57,7 +57,8 @@ extern "C" int laya_b200_attention(const void* qkv, void* out, int rows, int B, 
     if (!d.ready) {
       if (attn_tc_prepare_device() != cudaSuccess) return -4;
       if (cudaMalloc(&d.err, sizeof(int)) != cudaSuccess) return -4;
-      if (cudaMalloc(&d.ticket, sizeof(int)) != cudaSuccess) return -4;
+      if (cudaMalloc(&d.ticket, 2 * sizeof(int)) != cudaSuccess) return -4;
+      if (cudaMemset(d.ticket, 0, 2 * sizeof(int)) != cudaSuccess) return -4;
       if (cudaMemset(d.err, 0, sizeof(int)) != cudaSuccess) return -4;
       d.ready = true;
     }

@@ -59,6 +59,8 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const AttnArgs a) {
   __shared__ __align__(128) uint8_t sV[2][64 * 128];
   __shared__ int s_src[64], s_dst[64];
 
+  pdl_trigger();
+  pdl_wait();
   const AttnItem it = a.items[blockIdx.x];
   if (it.seq < 0) return;
   const int h = blockIdx.y;
@@ -238,6 +240,8 @@ template <bool GATHER>
 __global__ void __launch_bounds__(64) attn_f32_kernel(const AttnArgs a) {
   __shared__ __align__(16) float sK[32][64];
   __shared__ __align__(16) float sV[32][64];
+  pdl_trigger();
+  pdl_wait();
   const AttnItem it = a.items[blockIdx.x];
   if (it.seq < 0) return;
   const int h = blockIdx.y, D = a.H * 64, tid = threadIdx.x;
@@ -329,17 +333,15 @@ __global__ void __launch_bounds__(64) attn_f32_kernel(const AttnArgs a) {
 cudaError_t attn_bf16_launch(const AttnArgs& a, cudaStream_t st) {
   if (a.n_items <= 0) return cudaSuccess;
   dim3 grid(a.n_items, a.H);
-  if (a.gathered) attn_bf16_kernel<true><<<grid, 128, 0, st>>>(a);
-  else attn_bf16_kernel<false><<<grid, 128, 0, st>>>(a);
-  return cudaGetLastError();
+  if (a.gathered) return launch_pdl(attn_bf16_kernel<true>, grid, dim3(128), 0, st, a);
+  return launch_pdl(attn_bf16_kernel<false>, grid, dim3(128), 0, st, a);
 }
 
 cudaError_t attn_f32_launch(const AttnArgs& a, cudaStream_t st) {
   if (a.n_items <= 0) return cudaSuccess;
   dim3 grid(a.n_items, a.H);
-  if (a.gathered) attn_f32_kernel<true><<<grid, 64, 0, st>>>(a);
-  else attn_f32_kernel<false><<<grid, 64, 0, st>>>(a);
-  return cudaGetLastError();
+  if (a.gathered) return launch_pdl(attn_f32_kernel<true>, grid, dim3(64), 0, st, a);
+  return launch_pdl(attn_f32_kernel<false>, grid, dim3(64), 0, st, a);
 }
 
 }  // namespace laya

@@ -189,6 +189,7 @@ __device__ __forceinline__ bool take_unit(AttnSmem& S, int ui, Unit& u, volatile
 __global__ void __launch_bounds__(kThreads, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv, const AttnArgs a,
                    int* ticket, int* err) {
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   AttnSmem& S = *reinterpret_cast<AttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -223,6 +224,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = S.tmem;
+  pdl_wait();  // qkv (and the work counter's reset by the previous launch) are complete
   volatile int* abort = &S.abort;
 
   if (warp == 0) {
@@ -504,6 +506,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+  // The last CTA out resets the work counter for the next launch: every CTA has made its final
+  // claim before it counts itself out.
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(ticket + 1, 1) == static_cast<int>(gridDim.x) - 1) {
+      ticket[0] = 0;
+      ticket[1] = 0;
+      __threadfence();
+    }
+  }
 }
 
 int g_num_sms = 0;
@@ -523,13 +535,10 @@ cudaError_t attn_tc_prepare_device() {
 cudaError_t attn_tc_launch(const CUtensorMap& tq, const CUtensorMap& tkv, const AttnArgs& a, int* ticket, int* err,
                            cudaStream_t st) {
   if (a.gathered || a.out_planes != 1 || a.n_items <= 0 || a.H <= 0 || !ticket) return cudaErrorInvalidValue;
-  cudaError_t e = cudaMemsetAsync(ticket, 0, sizeof(int), st);  // the work counter starts at zero
-  if (e != cudaSuccess) return e;
   const int work = a.n_items * a.H;
   const int sms = g_num_sms > 0 ? g_num_sms : 148;
   const int grid = work < 2 * sms ? work : 2 * sms;
-  attn_tc_kernel<<<grid, kThreads, attn_smem_bytes(), st>>>(tq, tkv, a, ticket, err);
-  return cudaGetLastError();
+  return launch_pdl(attn_tc_kernel, dim3(grid), dim3(kThreads), attn_smem_bytes(), st, tq, tkv, a, ticket, err);
 }
 
 }  // namespace laya

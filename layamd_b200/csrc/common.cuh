@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <cstdlib>
+#include <utility>
 
 namespace laya {
 
@@ -21,6 +23,40 @@ enum DevErr : int {
   kErrAttnMma = 17,      // attention MMA issuer timed out waiting for Q / K / V / P
   kErrAttnSoftmax = 18,  // attention softmax warps timed out waiting for S or O
 };
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// With LAYA_PDL=1 every kernel of the pass is launched with programmatic stream serialization: the
+// next kernel on the stream may be scheduled as soon as all blocks of the current one have started
+// (pdl_trigger at their top), so its launch and prologue (barrier set-up, TMEM allocation) overlap
+// the current kernel's tail. Each kernel calls pdl_wait() before its first global-memory access,
+// which returns once the previous kernel has completed and its writes are visible (completion is
+// transitive along the stream); without the attribute both are no-ops. Off by default: measured on
+// the C2 pass and at batch 1 it made no difference outside run-to-run noise.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("LAYA_PDL");
+    return v && *v && atoi(v) != 0;
+  }();
+  return on;
+}
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ~2^31 SM cycles (~1 s at 1.9 GHz): far beyond any legitimate wait inside one tile.
 constexpr long long kWaitBudgetCycles = 1ll << 31;

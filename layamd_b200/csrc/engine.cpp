@@ -857,6 +857,8 @@ class Replica {
         *herr = 0;
         // an aborted split-K launch can leave tile counters part-way: clear them for the next pass
         if (counters) cudaMemset(counters, 0, n_counters * 4);
+        // and an aborted attention launch its work / exit counters
+        if (d_attn_ticket) cudaMemset(d_attn_ticket, 0, 16);
       }
       (void)cudaGetLastError();
       return -2;

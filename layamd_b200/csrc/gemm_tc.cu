@@ -243,6 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kIdesc = idesc_bf16(kBM, BN);
   constexpr uint32_t kStageBytes = (kBM + BN) * kBK * 2;
   using Smem = GemmSmem<BN, STAGES>;
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   Smem& S = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -267,6 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = S.tmem;
+  pdl_wait();  // the previous kernel's outputs (this GEMM's A operand, the residual) are complete
   volatile int* abort = &S.abort;
 
   if (warp == 0) {
@@ -475,6 +477,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   constexpr int BN = 256;
   constexpr uint32_t kIdesc = idesc_bf16(256, BN);
   constexpr uint32_t kPairStageBytes = 2u * (128 + 128) * kBK * 2;  // both CTAs' A and B halves
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   GemmSmemPair& S =
       *reinterpret_cast<GemmSmemPair*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -500,6 +503,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // both CTAs' barriers are initialised before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem = S.tmem;
+  pdl_wait();  // the previous kernel's outputs (this GEMM's A operand, the residual) are complete
   volatile int* abort = &S.abort;
 
   if (warp == 0) {
@@ -632,9 +636,9 @@ cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   const int work = ((sh.M + kBM - 1) / kBM) * ((sh.N + BN - 1) / BN) * (sh.splits > 1 ? sh.splits : 1);
   const int grid = work < grid_ctas ? work : grid_ctas;
   if (grid <= 0) return cudaSuccess;
-  if (sh.splits > 1) gemm_tc_kernel<BN, EPI, true><<<grid, kThreads, smem, st>>>(ta, tb, tc, sh, ep, err);
-  else gemm_tc_kernel<BN, EPI, false><<<grid, kThreads, smem, st>>>(ta, tb, tc, sh, ep, err);
-  return cudaGetLastError();
+  if (sh.splits > 1)
+    return launch_pdl(gemm_tc_kernel<BN, EPI, true>, dim3(grid), dim3(kThreads), smem, st, ta, tb, tc, sh, ep, err);
+  return launch_pdl(gemm_tc_kernel<BN, EPI, false>, dim3(grid), dim3(kThreads), smem, st, ta, tb, tc, sh, ep, err);
 }
 
 template <int BN>
@@ -674,8 +678,8 @@ cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   const int tiles = ((sh.M + 255) / 256) * ((sh.N + 255) / 256);
   const int ncl = tiles < clusters ? tiles : clusters;
   if (ncl <= 0) return cudaSuccess;
-  gemm_tc_pair_kernel<EPI><<<2 * ncl, kThreads, gemm_pair_smem_bytes(), st>>>(ta, tb, tc, sh, ep, err);
-  return cudaGetLastError();
+  return launch_pdl(gemm_tc_pair_kernel<EPI>, dim3(2 * ncl), dim3(kThreads), gemm_pair_smem_bytes(), st, ta, tb, tc, sh,
+                    ep, err);
 }
 
 }  // namespace

@@ -121,8 +121,8 @@ cudaError_t attn_f32_launch(const AttnArgs& a, cudaStream_t st);
 
 // tcgen05 attention (bf16, contiguous mode only): items are 128-query tiles (q0 a multiple of 128)
 // holding {seq, q0, first packed row, length}, longest sequences first (the persistent CTAs claim
-// (item, head) units in that order from the counter `ticket`, one device int that the launcher
-// zeroes on the stream); `tq` / `tkv` are make_operand_map over the qkv rows (K = 3*D, rows, 1 plane)
+// (item, head) units in that order from `ticket`: two device ints, zero before the first launch and
+// reset to zero by the last CTA of every launch); `tq` / `tkv` are make_operand_map over the qkv rows (K = 3*D, rows, 1 plane)
 // with 128-row and 64-row boxes; out is one bf16 plane [rows, D]. The K / V rows read past a
 // sequence's end must hold finite values. Bounded waits record an error code in *err.
 // attn_tc_prepare_device() runs once per device first.

@@ -52,6 +52,8 @@ __device__ __forceinline__ void layer_norm_regs(float4 (&v)[NV], const float* w,
 
 template <int NV>
 __global__ void __launch_bounds__(256) ln_kernel(const LnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
   if (row >= a.rows) return;
@@ -106,6 +108,8 @@ __global__ void __launch_bounds__(256) head_out_kernel(const HeadOutArgs a) {
   __shared__ float s_logit[256];
   __shared__ float s_in[1024 + 8];
   __shared__ float s_hid[256];
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int D = a.D, nm = a.nmark[b], mo = a.moff[b];
   // scorer output Linear(d, 1) at every option marker of this question
@@ -171,23 +175,21 @@ cudaError_t ln_launch(const LnArgs& a, cudaStream_t st) {
   if (a.D % 128 != 0 || a.D > 1024) return cudaErrorInvalidValue;
   const int grid = (a.rows + 7) / 8;
   switch (a.D / 128) {
-    case 1: ln_kernel<1><<<grid, 256, 0, st>>>(a); break;
-    case 2: ln_kernel<2><<<grid, 256, 0, st>>>(a); break;
-    case 3: ln_kernel<3><<<grid, 256, 0, st>>>(a); break;
-    case 4: ln_kernel<4><<<grid, 256, 0, st>>>(a); break;
-    case 5: ln_kernel<5><<<grid, 256, 0, st>>>(a); break;
-    case 6: ln_kernel<6><<<grid, 256, 0, st>>>(a); break;
-    case 7: ln_kernel<7><<<grid, 256, 0, st>>>(a); break;
-    case 8: ln_kernel<8><<<grid, 256, 0, st>>>(a); break;
+    case 1: return launch_pdl(ln_kernel<1>, dim3(grid), dim3(256), 0, st, a);
+    case 2: return launch_pdl(ln_kernel<2>, dim3(grid), dim3(256), 0, st, a);
+    case 3: return launch_pdl(ln_kernel<3>, dim3(grid), dim3(256), 0, st, a);
+    case 4: return launch_pdl(ln_kernel<4>, dim3(grid), dim3(256), 0, st, a);
+    case 5: return launch_pdl(ln_kernel<5>, dim3(grid), dim3(256), 0, st, a);
+    case 6: return launch_pdl(ln_kernel<6>, dim3(grid), dim3(256), 0, st, a);
+    case 7: return launch_pdl(ln_kernel<7>, dim3(grid), dim3(256), 0, st, a);
+    default: return launch_pdl(ln_kernel<8>, dim3(grid), dim3(256), 0, st, a);
   }
-  return cudaGetLastError();
 }
 
 cudaError_t head_out_launch(const HeadOutArgs& a, cudaStream_t st) {
   if (a.B <= 0) return cudaSuccess;
   if (a.D > 1024 || a.n_act > 256) return cudaErrorInvalidValue;
-  head_out_kernel<<<a.B, 256, 0, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(head_out_kernel, dim3(a.B), dim3(256), 0, st, a);
 }
 
 }  // namespace laya
