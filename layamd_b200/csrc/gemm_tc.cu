@@ -49,7 +49,7 @@ constexpr size_t gemm_smem_bytes() {
 
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == ACT_RELU) return fmaxf(v, 0.f);
-  if (act == ACT_GELU) return gelu_erf(v);
+  if (act == ACT_GELU) return gelu_as(v);
   return v;
 }
 
@@ -156,7 +156,7 @@ __device__ __forceinline__ void epilogue_tile(const Loader& ld, int row0, int la
         ld(s + c, xin);
         ld(s + 64 + c, gate);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[c + i] = gelu_erf(xin[i]) * gate[i];
+        for (int i = 0; i < 32; ++i) v[c + i] = gelu_as(xin[i]) * gate[i];
       }
       emit64(stg, lane, out_map, ep.out_mode, v, ocol, row0);
     }
