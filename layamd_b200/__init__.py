@@ -88,6 +88,7 @@ class Engine:
         self.n_act = L.laya_n_act(self.h)
         self.max_markers = L.laya_max_markers(self.h)
         self.max_len = L.laya_max_len(self.h)
+        self.num_devices = L.laya_num_devices(self.h)
 
     def close(self):
         if self.h:

@@ -129,6 +129,52 @@ def agent_config(a: Arch):
             "amp_dtype": "bf16"}
 
 
+# ---- synthetic tokenizer (the request path's tests and benchmark; real checkpoints ship their own).
+# A word-level vocabulary over the words the request layout itself writes ("choice question:",
+# "level 0:", the yes/no option texts, JSON punctuation runs) plus everyday words and numbers, then
+# filler tokens "t<id>" up to the model's vocabulary size; [MASK] / [CLS] / [SEP] / [PAD] sit at the
+# architecture's special ids and [UNK] at the lowest free id. Pre-tokenisation splits on whitespace
+# and punctuation runs, so one word is one token and sequence lengths are easy to control.
+_TOKEN_WORDS = (
+    "choice score noul question level false true no yes the statement does not hold holds is a an of to in it and "
+    "or for on with as at by this that be are was were has have had will would can could should may might what which "
+    "who how when where why user agent state goal task step action next best open closed door light room key box item "
+    "table chair left right up down move pick drop wait go stop done ready safe unsafe good bad high low red green blue "
+    "answer response correct wrong helpful relevant quality rate reached found empty full true_ false_ "
+    "0 1 2 3 4 5 6 7 8 9 10 11 12 13 14 15 16 17 18 19 20 100 1000").split() + [
+    ":", ",", ".", "?", "!", "-", "(", ")", "/", "'", '"', "{", "}", "[", "]", '{"', '":', '",', '"}', '"]', '["',
+    '":"', '","', '"},', "},", "}}", "]}", "\\"]
+
+
+def tokenizer_vocab(a: Arch) -> Dict[str, int]:
+    special = {"[MASK]": a.mask_id, "[CLS]": a.cls_id, "[SEP]": a.sep_id, "[PAD]": a.pad_id}
+    taken = set(special.values())
+    words = ["[UNK]"] + list(dict.fromkeys(_TOKEN_WORDS))
+    vocab = dict(special)
+    i = 0
+    for idx in range(a.vocab):  # dense ids: the tokenizers library warns about holes
+        if idx in taken:
+            continue
+        vocab[words[i] if i < len(words) else "t%d" % idx] = idx
+        i += 1
+    return vocab
+
+
+def write_tokenizer(out_dir: str, a: Arch):
+    """Writes tokenizer.json and tokenizer_config.json (the files the request path loads) into out_dir."""
+    from tokenizers import Tokenizer, models, pre_tokenizers
+
+    os.makedirs(out_dir, exist_ok=True)
+    t = Tokenizer(models.WordLevel(vocab=tokenizer_vocab(a), unk_token="[UNK]"))
+    t.pre_tokenizer = pre_tokenizers.Whitespace()
+    t.add_special_tokens(["[MASK]", "[CLS]", "[SEP]", "[PAD]"])
+    tmp = os.path.join(out_dir, "tokenizer.json.tmp")
+    t.save(tmp)
+    os.replace(tmp, os.path.join(out_dir, "tokenizer.json"))
+    with open(os.path.join(out_dir, "tokenizer_config.json"), "w") as f:
+        json.dump({"mask_token": "[MASK]", "cls_token": "[CLS]", "sep_token": "[SEP]", "pad_token": "[PAD]"}, f)
+
+
 def default_root():
     return os.environ.get("LAYA_SYNTH_DIR", "/tmp/laya_synth")
 
@@ -141,6 +187,8 @@ def checkpoint(arch: str, seed: int = 0, root: str = None) -> str:
     d = os.path.join(root, "%s-s%d-%s" % (arch, seed, key))
     done = os.path.join(d, ".complete")
     if os.path.exists(done):
+        if not os.path.exists(os.path.join(d, "tokenizer", "tokenizer.json")):
+            write_tokenizer(os.path.join(d, "tokenizer"), a)
         return d
     os.makedirs(os.path.join(d, "encoder"), exist_ok=True)
     wsrc = WEIGHTS_OF.get(arch)
@@ -158,6 +206,7 @@ def checkpoint(arch: str, seed: int = 0, root: str = None) -> str:
         json.dump(encoder_config(a), f, indent=1)
     with open(os.path.join(d, "rl_agent_config.json"), "w") as f:
         json.dump(agent_config(a), f, indent=1)
+    write_tokenizer(os.path.join(d, "tokenizer"), a)
     open(done, "w").close()
     return d
 
