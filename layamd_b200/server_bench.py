@@ -11,6 +11,8 @@ Measured, one JSON line:
            (decisions/s, request latency p50 / p99, rounds and tokens per round)
   host     prepare + finish alone per request (CPU time of the request path around the engine)
   engine   all 192 questions in one ``forward_batch`` (the engine-only rate for the same inputs)
+  many     64 choice questions of 120 options each (300-token states) in one ``forward_batch``: the
+           gathered marker rows (7,680) dominate the last head layer and the scorer
 
     python -m layamd_b200.server_bench [--clients 64] [--seconds 20] [--devices 0,1]
 """
@@ -133,6 +135,20 @@ def main():
     wall = time.perf_counter() - t
     b.close()
     all_lat = [x for l_ in blat for x in l_]
+
+    # many options: 64 questions of 120 options each (7,680 marker rows in gathered tiles) in one call
+    rng = np.random.default_rng(120)
+    many = []
+    for i in range(64):
+        crit = {"t%d" % (3000 + j): "queue t%d" % rng.integers(2000, 40000) for j in range(120)}
+        state = " ".join("t%d" % v for v in rng.integers(2000, 40000, 300))
+        many.append(lay.prepare(state, {"q": {"type": "choice", "instructions": "which queue?", "criteria": crit}})[2][0])
+    ms, mm, mq = [x[0] for x in many], [x[1] for x in many], [x[2] for x in many]
+    lay.engine.forward_batch(ms, mm, mq)
+    t = time.perf_counter()
+    for _ in range(reps):
+        lay.engine.forward_batch(ms, mm, mq)
+    many_rate = reps * len(many) / (time.perf_counter() - t)
     out = {
         "metric": "request-path decisions/sec (ModernBERT-large, C2 requests: state + 3 questions)",
         "workload": "C2 as requests: 64 states, L~U[32,512], 3 questions each (%d tokens)" % tokens,
@@ -146,6 +162,8 @@ def main():
                     "rounds": b.stats["passes"], "max_tokens": b.max_tokens,
                     "tokens_per_round": round(b.stats["tokens"] / max(1, b.stats["passes"]), 1),
                     "questions_per_round": round(b.stats["questions"] / max(1, b.stats["passes"]), 1)},
+        "many_options": {"decisions_per_s": round(many_rate, 1), "questions": len(many), "options": 120,
+                         "tokens_per_question": len(ms[0]), "call": "all questions in one forward_batch"},
         "host": {"prepare_ms_per_request": round(t_prep * 1e3, 3), "finish_ms_per_request": round(t_fin * 1e3, 3)},
         "graphs": os.environ.get("LAYA_GRAPHS", "1"),
     }

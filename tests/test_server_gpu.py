@@ -107,3 +107,56 @@ def test_batcher_rounds_match_direct_calls(tiny, golden):
     assert b.stats["questions"] == sum(len(c["qids"]) for c in reqs)
     for a, d in zip(got, direct):
         close_answers(a, d, 2e-4)
+
+
+# ---------------------------------------------------------------- many options (row f3)
+@pytest.fixture(scope="module")
+def large():
+    ck = synth.checkpoint("large", 0)
+    lay = S.Laya(ck, warmup=False)  # bf16 engine
+    yield ck, lay
+    lay.engine.close()
+
+
+def many_option_requests():
+    """Two 77-option and one 120-option choice questions (ticket routing style), 300-token states."""
+    rng = np.random.default_rng(77)
+    reqs = []
+    for n in (77, 77, 120):
+        crit = {"t%d" % (3000 + 7 * i + n): "queue t%d t%d" % tuple(rng.integers(2000, 40000, 2)) for i in range(n)}
+        state = " ".join("t%d" % v for v in rng.integers(2000, 40000, 300))
+        reqs.append((state, {"q": {"type": "choice", "instructions": "which queue should take this ticket?",
+                                   "criteria": crit}}))
+    return reqs
+
+
+def test_many_options_match_oracle(large):
+    """Questions with more options than one 64-row marker tile, all in one engine call (274 marker rows
+    over several gathered tiles), on ModernBERT-large in bf16 through the request path: every
+    probability within 0.01 of the fp32 oracle's and the same argmax wherever the oracle's top-2
+    logit gap exceeds 2e-3 (the tolerance of the reference's many-option check,
+    bench/eval/check_many_options.py)."""
+    ck, lay = large
+    o = om.Oracle(synth.load_weights(ck), synth.load_arch(ck))
+    reqs = many_option_requests()
+    prepared = [lay.prepare(s, q) for s, q in reqs]
+    items = [it[0] for _, _, it in prepared]
+    lg, ac = lay.engine.forward_batch([i[0] for i in items], [i[1] for i in items], [i[2] for i in items])
+    lo_o, ac_o, _ = o.forward_batch([{"ids": s, "markers": m, "qtype": t} for s, m, t in items])
+    off = 0
+    for (qids, qs, it), got in zip(prepared, lg):
+        k = len(it[0][1])
+        want = np.asarray(lo_o[off:off + k], np.float64)
+        off += k
+        assert len(got) == k == len(qs[0]["crit"])
+        pg, pw = S._softmax(np.asarray(got, np.float64)), S._softmax(want)
+        assert np.abs(pg - pw).max() < 0.01
+        top = np.sort(want)[::-1]
+        if top[0] - top[1] > 2e-3:
+            assert int(np.argmax(got)) == int(np.argmax(want))
+    assert np.abs(np.asarray(ac, np.float64) - np.asarray(ac_o, np.float64)).max() < 0.05 * np.abs(ac_o).max()
+    # the same questions as requests give the same probabilities as the single call
+    for (s, q), (qids, qs, it), got in zip(reqs, prepared, lg):
+        ans = lay.system_one(s, q)["answers"]["q"]["probabilities"]
+        p = S._softmax(np.asarray(got, np.float64) / lay.temperature[0])
+        assert max(abs(ans[kk] - float(v)) for kk, v in zip(qs[0]["crit"], p)) <= 2e-3
