@@ -10,10 +10,11 @@ sequence layout, truncation rules, temperature buckets and answer format are the
 checkpoints were trained on that layout and its clients parse that format); the HTTP layer is not
 part of this module.
 
-B200 choices: the batching worker hands the engine rounds of up to the engine's pass capacity times
-its GPU count (65536 tokens per GPU by default) instead of 4096 tokens, so one round fills every
-GPU's pass; a request's question headers are tokenised in one batched call; and the worker can be
-stopped (``Batcher.close``).
+B200 choices: the batching worker hands the engine rounds of up to 65536 tokens per GPU of the
+handle instead of 4096 tokens (a B200 pass reaches its full rate at about 16k tokens; 65536 keeps a
+round's latency near one C2-size pass), so concurrent requests share passes on every GPU; a request's
+question headers are tokenised in one batched call; and the worker can be stopped
+(``Batcher.close``).
 """
 import functools
 import itertools
@@ -30,7 +31,7 @@ import numpy as np
 QTYPES = {"choice": 0, "score": 1, "noul": 2}
 QTYPE_NAMES = {v: k for k, v in QTYPES.items()}
 OPTION_TOKENS = 48  # tokens kept per rendered option after its [MASK] (laya_server.py:79)
-DEFAULT_PASS_TOKENS = 65536  # tokens per GPU per batching round (the engine's default pass capacity)
+DEFAULT_PASS_TOKENS = 65536  # tokens per GPU per batching round
 
 
 # ------------------------------------------------------------------ sequence construction
