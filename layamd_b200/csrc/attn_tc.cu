@@ -11,10 +11,10 @@
 //               ring in shared memory; the unit's Q tile into one of two Q slots, then 64-key K and V tiles
 //               into a 4-stage ring (a stage is released when its PV is done), running ahead into
 //               the next units
-//   warp 1      TMEM owner + MMA issuer: S = Q K^T (128 x 64 fp32, two TMEM buffers so S(c+1) is
-//               formed while the softmax of chunk c runs) and O += P V (128 x 64 fp32 in TMEM; P is
-//               the A operand read from tensor memory, V the B operand read MN-major from its TMA
-//               tile)
+//   warp 1      TMEM owner + MMA issuer: S = Q K^T (128 x 64 fp32 in one TMEM buffer; S(c+1) is
+//               issued as soon as the softmax warps have copied S(c) into registers, so it forms
+//               while the softmax of chunk c runs) and O += P V (128 x 64 fp32 in TMEM; P is the A
+//               operand read from tensor memory, V the B operand read MN-major from its TMA tile)
 //   warps 2..5  softmax, one query row per thread (the row's TMEM lane), one pass over the 64 scores
 //               of a chunk: mask, row max, p = 2^(s*c - m), row sum, P as bf16 pairs into one of two
 //               TMEM buffers. The reference max m is only raised (and O rescaled in TMEM, which waits
