@@ -104,26 +104,58 @@ __global__ void __launch_bounds__(256) ln_kernel(const LnArgs a) {
   }
 }
 
+// One warp: the dot product of a D-element row (fp32 or bf16, 16-byte aligned, D a multiple of 128
+// and at most 1024) with the fp32 vector w. Every load of the lane is issued before the first use.
+__device__ __forceinline__ float row_dot(const void* row, bool f32, const float* w, int D, int lane) {
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float s = 0.f;
+  if (f32) {
+    const float4* r4 = static_cast<const float4*>(row);
+    float4 x[8], y[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (lane + 32 * i < D / 4) { x[i] = r4[lane + 32 * i]; y[i] = w4[lane + 32 * i]; }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (lane + 32 * i < D / 4) s += (x[i].x * y[i].x + x[i].y * y[i].y) + (x[i].z * y[i].z + x[i].w * y[i].w);
+  } else {
+    const uint4* r8 = static_cast<const uint4*>(row);
+    uint4 x[4];
+    float4 y[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (lane + 32 * i < D / 8) {
+        x[i] = r8[lane + 32 * i];
+        y[2 * i] = w4[2 * (lane + 32 * i)];
+        y[2 * i + 1] = w4[2 * (lane + 32 * i) + 1];
+      }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (lane + 32 * i < D / 8) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x[i]);
+        const float2 f0 = __bfloat1622float2(h[0]), f1 = __bfloat1622float2(h[1]);
+        const float2 f2 = __bfloat1622float2(h[2]), f3 = __bfloat1622float2(h[3]);
+        s += (f0.x * y[2 * i].x + f0.y * y[2 * i].y) + (f1.x * y[2 * i].z + f1.y * y[2 * i].w) +
+             ((f2.x * y[2 * i + 1].x + f2.y * y[2 * i + 1].y) + (f3.x * y[2 * i + 1].z + f3.y * y[2 * i + 1].w));
+      }
+  }
+  return warp_sum(s);
+}
+
 __global__ void __launch_bounds__(256) head_out_kernel(const HeadOutArgs a) {
   __shared__ float s_logit[256];
-  __shared__ float s_in[1024 + 8];
+  __shared__ __align__(16) float s_in[1024 + 8];
   __shared__ float s_hid[256];
   pdl_trigger();
   pdl_wait();
   const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int D = a.D, nm = a.nmark[b], mo = a.moff[b];
-  // scorer output Linear(d, 1) at every option marker of this question
+  // scorer output Linear(d, 1) at every option marker of this question, one warp per marker
   for (int k = warp; k < nm; k += 8) {
     const long long row = mo + k;
-    float s = 0.f;
-    if (a.hs_f32) {
-      const float* hr = static_cast<const float*>(a.hs) + row * D;
-      for (int i = lane; i < D; i += 32) s = fmaf(hr[i], a.w3[i], s);
-    } else {
-      const bf16* hr = static_cast<const bf16*>(a.hs) + row * D;
-      for (int i = lane; i < D; i += 32) s = fmaf(__bfloat162float(hr[i]), a.w3[i], s);
-    }
-    s = warp_sum(s) + a.b3;
+    const void* hr = a.hs_f32 ? static_cast<const void*>(static_cast<const float*>(a.hs) + row * D)
+                              : static_cast<const void*>(static_cast<const bf16*>(a.hs) + row * D);
+    const float s = row_dot(hr, a.hs_f32 != 0, a.w3, D, lane) + a.b3;
     if (lane == 0) {
       s_logit[k] = s;
       a.logits[mo + k] = s;
@@ -150,19 +182,41 @@ __global__ void __launch_bounds__(256) head_out_kernel(const HeadOutArgs a) {
     s_in[D + 3] = k / 255.f;
   }
   __syncthreads();
-  const int K0 = D + 4;
-  for (int j = warp; j < 256; j += 8) {
-    const float* wr = a.w0 + (long long)j * K0;
-    float s = 0.f;
-    for (int i = lane; i < K0; i += 32) s = fmaf(wr[i], s_in[i], s);
-    s = warp_sum(s);
-    if (lane == 0) s_hid[j] = gelu_erf(s + a.b0[j]);
+  // act head hidden layer: 256 rows of D + 4 weights, two rows per step of each warp with all of the
+  // lane's (at most nine) 16-byte pieces of both rows in flight together
+  const int K4 = (D + 4) / 4;  // D + 4 is a multiple of 4: every row starts 16-byte aligned
+  const float4* s4 = reinterpret_cast<const float4*>(s_in);
+  for (int j = warp * 32; j < warp * 32 + 32; j += 2) {
+    const float4* r0 = reinterpret_cast<const float4*>(a.w0) + (long long)j * K4;
+    const float4* r1 = r0 + K4;
+    float4 w0[9], w1[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i)
+      if (lane + 32 * i < K4) { w0[i] = r0[lane + 32 * i]; w1[i] = r1[lane + 32 * i]; }
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 9; ++i)
+      if (lane + 32 * i < K4) {
+        const float4 x = s4[lane + 32 * i];
+        s0 += (w0[i].x * x.x + w0[i].y * x.y) + (w0[i].z * x.z + w0[i].w * x.w);
+        s1 += (w1[i].x * x.x + w1[i].y * x.y) + (w1[i].z * x.z + w1[i].w * x.w);
+      }
+    s0 = warp_sum(s0);
+    s1 = warp_sum(s1);
+    if (lane == 0) {
+      s_hid[j] = gelu_erf(s0 + a.b0[j]);
+      s_hid[j + 1] = gelu_erf(s1 + a.b0[j + 1]);
+    }
   }
   __syncthreads();
   for (int j = warp; j < a.n_act; j += 8) {
     const float* wr = a.w2 + (long long)j * 256;
+    float x[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = wr[lane + 32 * i];
     float s = 0.f;
-    for (int i = lane; i < 256; i += 32) s = fmaf(wr[i], s_hid[i], s);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s = fmaf(x[i], s_hid[lane + 32 * i], s);
     s = warp_sum(s);
     if (lane == 0) a.act[(long long)b * a.n_act + j] = s + a.b2[j];
   }
@@ -188,7 +242,7 @@ cudaError_t ln_launch(const LnArgs& a, cudaStream_t st) {
 
 cudaError_t head_out_launch(const HeadOutArgs& a, cudaStream_t st) {
   if (a.B <= 0) return cudaSuccess;
-  if (a.D > 1024 || a.n_act > 256) return cudaErrorInvalidValue;
+  if (a.D > 1024 || a.D % 128 != 0 || a.n_act > 256) return cudaErrorInvalidValue;  // 16-byte row pieces
   return launch_pdl(head_out_kernel, dim3(a.B), dim3(256), 0, st, a);
 }
 
