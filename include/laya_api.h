@@ -123,9 +123,9 @@ int laya_b200_gemm(const void* A, const void* W, void* out, float* resid, const 
 
 /* laya_b200_gemm with the K loop split into `splits` slices (1..8) run by different CTAs, for small M
  * where the output tiles alone cannot fill the GPU (one-CTA tiles, bn 128 or 256). The fp32 partials
- * go to a workspace the library allocates on the device and keeps for later calls; the last slice
- * of each tile sums them in slice order, so results do not depend on scheduling. Calls that overlap
- * on the GPU (other streams) share that workspace and must not be issued. */
+ * go to a workspace the library allocates on the device and keeps for later calls; a second kernel
+ * sums them in slice order and applies the epilogue, so results do not depend on scheduling. Calls
+ * that overlap on the GPU (other streams) share that workspace and must not be issued. */
 int laya_b200_gemm_splitk(const void* A, const void* W, void* out, float* resid, const float* bias, int M, int N,
                           int K, int planes, int epi, int out_mode, int act, int bn, const float* cos_t,
                           const float* sin_t, const int* pos, int rope_cols, int geglu_I, int splits, void* stream,
@@ -147,12 +147,12 @@ int laya_b200_attention(const void* qkv, void* out, int rows, int B, const int* 
  * could fail, fragment the host's pool or stall every stream with its implicit synchronisation. Same
  * arguments and results; it calls no cudaMalloc or cudaFree. Its scratch is a fixed 16 MiB array in
  * the library's device image, held by every GPU that loads the library until the process exits:
- * splits x M x N must stay <= 4194304 fp32 partials and the 128-row tiles x 4 <= 4096 counters,
- * else the call prints why and returns -7 without launching. The first call on a device sets up
+ * splits x M x N must stay <= 4194304 fp32 partials, else the call prints why and returns -7
+ * without launching. The first call on a device sets up
  * (kernel attributes and the array's device address, no allocation); make it before any stream
  * capture. Every call on a device shares the array: calls that overlap on the GPU (other streams,
- * other threads) race and must not be issued. Each call clears the counters and error word it
- * inherits from the previous one. */
+ * other threads) race and must not be issued. Each call clears the error word it inherits from the
+ * previous one; every slice overwrites its whole plane of partials. */
 int laya_b200_gemm_splitk_noalloc(const void* A, const void* W, void* out, float* resid, const float* bias, int M,
                                   int N, int K, int planes, int epi, int out_mode, int act, int bn,
                                   const float* cos_t, const float* sin_t, const int* pos, int rope_cols,

@@ -14,8 +14,6 @@ struct DevState {
   int* err = nullptr;        // device error word
   float* ws = nullptr;       // split-K partials (grown on demand)
   size_t ws_floats = 0;
-  int* counters = nullptr;   // split-K tile counters (grown on demand, kept zero)
-  size_t n_counters = 0;
 };
 std::vector<DevState> g_dev;
 
@@ -35,11 +33,10 @@ int num_sms(int dev) {
   return n > 0 ? n : 1;
 }
 
-// Shared body of the GEMM entry points. ws / counters are used when splits > 1.
+// Shared body of the GEMM entry points. ws (splits x M x N fp32 partials) is used when splits > 1.
 int run_gemm(const void* A, const void* W, void* out, float* resid, const float* bias, int M, int N, int K, int planes,
              int epi, int out_mode, int act, int bn, const float* cos_t, const float* sin_t, const int* pos,
-             int rope_cols, int geglu_I, void* stream, int sync, int splits, float* ws, int* counters, int* err,
-             int dev) {
+             int rope_cols, int geglu_I, void* stream, int sync, int splits, float* ws, int* err, int dev) {
   using namespace laya;
   if ((planes != 1 && planes != 2) || M <= 0 || N <= 0 || K <= 0) return -2;
   if (bn != 128 && bn != 256 && bn != kGemmPair) return -2;
@@ -55,7 +52,8 @@ int run_gemm(const void* A, const void* W, void* out, float* resid, const float*
   GemmShape sh{M, N, K, planes == 2 ? 3 : 1};
   sh.splits = splits;
   sh.ws = ws;
-  sh.counters = counters;
+  sh.dst = dst;
+  sh.dst_plane = (long long)M * ncols;
   GemmEpi ep;
   ep.kind = epi;
   ep.out_mode = out_mode;
@@ -99,7 +97,7 @@ extern "C" int laya_b200_gemm(const void* A, const void* W, void* out, float* re
     err = d->err;
   }
   return run_gemm(A, W, out, resid, bias, M, N, K, planes, epi, out_mode, act, bn, cos_t, sin_t, pos, rope_cols,
-                  geglu_I, stream, sync, 1, nullptr, nullptr, err, dev);
+                  geglu_I, stream, sync, 1, nullptr, err, dev);
 }
 
 extern "C" int laya_b200_gemm_splitk(const void* A, const void* W, void* out, float* resid, const float* bias, int M,
@@ -111,14 +109,13 @@ extern "C" int laya_b200_gemm_splitk(const void* A, const void* W, void* out, fl
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;
   if (splits < 1 || splits > kMaxSplits || (splits > 1 && bn == kGemmPair) || M <= 0 || N <= 0) return -2;
   float* ws = nullptr;
-  int* counters = nullptr;
   int* err;
   {
     std::lock_guard<std::mutex> lk(g_mu);
     DevState* d = dev_state(dev);
     if (!d) return -4;
     err = d->err;
-    const size_t need_ws = splitk_ws_floats(M, N, splits), need_ct = splitk_counters(M, N, 128);
+    const size_t need_ws = splitk_ws_floats(M, N, splits);
     if (splits > 1 && d->ws_floats < need_ws) {
       if (d->ws) cudaFree(d->ws);
       d->ws = nullptr;
@@ -126,19 +123,10 @@ extern "C" int laya_b200_gemm_splitk(const void* A, const void* W, void* out, fl
       if (cudaMalloc(&d->ws, need_ws * sizeof(float)) != cudaSuccess) return -4;
       d->ws_floats = need_ws;
     }
-    if (splits > 1 && d->n_counters < need_ct) {
-      if (d->counters) cudaFree(d->counters);
-      d->counters = nullptr;
-      d->n_counters = 0;
-      if (cudaMalloc(&d->counters, need_ct * sizeof(int)) != cudaSuccess) return -4;
-      if (cudaMemset(d->counters, 0, need_ct * sizeof(int)) != cudaSuccess) return -4;
-      d->n_counters = need_ct;
-    }
     ws = d->ws;
-    counters = d->counters;
   }
   return run_gemm(A, W, out, resid, bias, M, N, K, planes, epi, out_mode, act, bn, cos_t, sin_t, pos, rope_cols,
-                  geglu_I, stream, sync, splits, ws, counters, err, dev);
+                  geglu_I, stream, sync, splits, ws, err, dev);
 }
 
 // ---------------------------------------------------------------- split-K with no allocation
@@ -146,15 +134,13 @@ extern "C" int laya_b200_gemm_splitk(const void* A, const void* W, void* out, fl
 // let a library do it: a host whose memory manager reserves the GPU's memory up front (a serving
 // stack with a caching allocator, where a cudaMalloc from outside can fail or fragment its pool),
 // or a plugin host that forbids allocation inside its callbacks, where cudaMalloc's implicit device
-// synchronisation would also stall every other stream. Its scratch (split-K partials, tile
-// counters, error word) is this fixed array in the library's device image instead: every GPU that
-// loads the library holds its 16 MiB until the process exits, and every call on a device shares it.
+// synchronisation would also stall every other stream. Its scratch (split-K partials, error word)
+// is this fixed array in the library's device image instead: every GPU that loads the library holds
+// its 16 MiB until the process exits, and every call on a device shares it.
 namespace {
 constexpr size_t kNoAllocWsFloats = size_t(4) << 20;  // fp32 partials: splits x M x N <= 4 Mi (16 MiB)
-constexpr size_t kNoAllocCounters = 4096;              // one per (128-row tile, 32-row quarter)
 constexpr size_t kNoAllocWsBytes = kNoAllocWsFloats * sizeof(float);
-constexpr size_t kNoAllocCtBytes = kNoAllocCounters * sizeof(int);
-constexpr size_t kNoAllocBytes = kNoAllocWsBytes + kNoAllocCtBytes + 256;  // + the error word
+constexpr size_t kNoAllocBytes = kNoAllocWsBytes + 256;  // + the error word
 constexpr int kNoAllocMaxDevices = 64;
 }  // namespace
 
@@ -195,12 +181,11 @@ extern "C" int laya_b200_gemm_splitk_noalloc(const void* A, const void* W, void*
   using namespace laya;
   if (splits < 1 || splits > kMaxSplits || (splits > 1 && bn == kGemmPair) || M <= 0 || N <= 0) return -2;
   const size_t need_ws = splits > 1 ? splitk_ws_floats(M, N, splits) : 0;
-  const size_t need_ct = splits > 1 ? splitk_counters(M, N, 128) : 0;
-  if (need_ws > kNoAllocWsFloats || need_ct > kNoAllocCounters) {
+  if (need_ws > kNoAllocWsFloats) {
     fprintf(stderr,
-            "[laya] laya_b200_gemm_splitk_noalloc: M %d x N %d in %d slices needs %zu partial floats and %zu "
-            "counters; the static scratch holds %zu and %zu (use laya_b200_gemm_splitk)\n",
-            M, N, splits, need_ws, need_ct, kNoAllocWsFloats, kNoAllocCounters);
+            "[laya] laya_b200_gemm_splitk_noalloc: M %d x N %d in %d slices needs %zu partial floats; the "
+            "static scratch holds %zu (use laya_b200_gemm_splitk)\n",
+            M, N, splits, need_ws, kNoAllocWsFloats);
     return -7;
   }
   int dev = 0;
@@ -209,12 +194,11 @@ extern "C" int laya_b200_gemm_splitk_noalloc(const void* A, const void* W, void*
   unsigned char* base = noalloc_scratch(dev);
   if (!base) return -4;
   float* ws = reinterpret_cast<float*>(base);
-  int* counters = reinterpret_cast<int*>(base + kNoAllocWsBytes);
-  int* err = reinterpret_cast<int*>(base + kNoAllocWsBytes + kNoAllocCtBytes);
-  // The array keeps whatever the last call (possibly an aborted one) left: the counters and the
-  // error word, which sit back to back, start every call at zero. The partials need no clearing.
+  int* err = reinterpret_cast<int*>(base + kNoAllocWsBytes);
+  // The array keeps whatever the last call (possibly an aborted one) left: the error word starts
+  // every call at zero. The partials need no clearing: every slice overwrites its whole plane.
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(counters, 0, kNoAllocCtBytes + sizeof(int), st) != cudaSuccess) return -5;
+  if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess) return -5;
   return run_gemm(A, W, out, resid, bias, M, N, K, planes, epi, out_mode, act, bn, cos_t, sin_t, pos, rope_cols,
-                  geglu_I, stream, sync, splits, ws, counters, err, dev);
+                  geglu_I, stream, sync, splits, ws, err, dev);
 }

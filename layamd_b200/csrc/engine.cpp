@@ -119,12 +119,10 @@ class Replica {
   Engine& E;
   const Config& cfg;
   int dev = 0, P = 1, nseg = 1, num_sms = 148, pair_clusters = 0;
-  // split-K workspace (fp32 partials) and its tile counters, sized at load
+  // split-K workspace (fp32 partials of every slice), sized at load
   float* ws = nullptr;
   size_t ws_floats = 0;
-  int* counters = nullptr;
-  size_t n_counters = 0;
-  bool use_splitk = false;
+  bool use_splitk = true;
   cudaStream_t st = nullptr;
   std::vector<void*> allocs;
   std::vector<void*> host_allocs;
@@ -390,17 +388,13 @@ class Replica {
     if (!dalloc(&d_act, (size_t)Bcap * cfg.n_act * 4, err)) return false;
     if (!dalloc(&d_err, 16, err)) return false;
     if (!dalloc(&d_attn_ticket, 16, err)) return false;
-    // Split-K (opt-in with LAYA_SPLITK=1): the last slice of each tile sums the workspace partials
-    // of all slices, a chain of L2 round trips that costs more than the idle SMs it recovers on the
-    // shapes measured so far, so the default keeps whole-K tiles. It is chosen only when the
-    // 128 x 128 tiles cannot fill the GPU, i.e. for a few thousand rows at most; 32 M floats
-    // (128 MB) covers every split count there.
-    use_splitk = getenv("LAYA_SPLITK") != nullptr && atoi(getenv("LAYA_SPLITK")) != 0;
+    // Split-K (LAYA_SPLITK=0 turns it off): when the 128 x 128 tiles of a GEMM cannot fill the
+    // GPU (a few thousand rows at most: batch-1 and small calls), its K loop is cut into slices
+    // whose partials a second kernel sums in order. 32 M floats (128 MB) cover every split count.
+    use_splitk = !(getenv("LAYA_SPLITK") && atoi(getenv("LAYA_SPLITK")) == 0);
     if (use_splitk) {
       ws_floats = (size_t)32 << 20;
       if (!dalloc(&ws, ws_floats * 4, err)) return false;
-      n_counters = splitk_counters(Tcap, std::max(std::max(2 * I, FF), 3 * D), 128);
-      if (!dalloc(&counters, n_counters * 4, err)) return false;
     }
     const MetaLayout L = meta_layout(Tcap, Bcap, Rcap);
     meta_cap = L.total;
@@ -528,7 +522,10 @@ class Replica {
     const long long t256 = (long long)((M + 127) / 128) * ((W.N + 255) / 256);
     return t256 >= 2LL * num_sms ? 256 : 128;
   }
-  void gemm(const Operand& A, int M, const Mat& W, const CUtensorMap& out, const GemmEpi& ep) {
+  // out: the epilogue's output map; dst / dst_plane: the buffer it covers (for a split-K launch,
+  // whose epilogue runs in a second kernel on plain pointers).
+  void gemm(const Operand& A, int M, const Mat& W, const CUtensorMap& out, void* dst, long long dst_plane,
+            const GemmEpi& ep) {
     int bn = pick_tile(M, W);
     GemmShape sh{M, W.N, W.K, nseg};
     if (bn == 128 && use_splitk) {
@@ -539,7 +536,8 @@ class Replica {
       if (s > 1) {
         sh.splits = s;
         sh.ws = ws;
-        sh.counters = counters;
+        sh.dst = dst;
+        sh.dst_plane = dst_plane;
       }
     }
     launched(gemm_launch(A.map, bn == 256 ? W.m256 : W.m128, out, bn, sh, ep, d_err, num_sms, st));
@@ -662,12 +660,12 @@ class Replica {
         e.sin_t = glob ? sin_g : sin_l;
         e.pos = pos;
         e.rope_cols = 2 * D;
-        gemm(xn, M, enc[l].Wqkv, out_qkv, e);
+        gemm(xn, M, enc[l].Wqkv, out_qkv, qkv, 0, e);
       });
       stage(glob ? "attn_global" : "attn_sliding", [&] {
         attend_rows(items, L.items_cap, items128, L.items128_cap, soff, slen, glob ? 0 : cfg.local_attention / 2);
       });
-      stage("gemm_attn_out", [&] { gemm(ao, M, enc[l].Wo, out_x, epi_resid(nullptr)); });
+      stage("gemm_attn_out", [&] { gemm(ao, M, enc[l].Wo, out_x, x, 0, epi_resid(nullptr)); });
       stage("ln", [&] {
         LnArgs a = ln_base(M);
         a.src = x;
@@ -680,9 +678,9 @@ class Replica {
         GemmEpi e = epi_store(act_mode(), nullptr, ACT_NONE);
         e.kind = EPI_GEGLU;
         e.geglu_I = I;
-        gemm(xn, M, enc[l].Wi, out_mg, e);
+        gemm(xn, M, enc[l].Wi, out_mg, mg.p, mg.plane, e);
       });
-      stage("gemm_mlp_out", [&] { gemm(mg, M, enc[l].Wmo, out_x, epi_resid(nullptr)); });
+      stage("gemm_mlp_out", [&] { gemm(mg, M, enc[l].Wmo, out_x, x, 0, epi_resid(nullptr)); });
       snprintf(nb, sizeof nb, "enc%d", l);
       dump(nb, x, p.T);
       stage("ln", [&] {
@@ -709,10 +707,10 @@ class Replica {
     for (int j = 0; j < HL; ++j) {
       const Head& h = head[j];
       const bool last = j == HL - 1;
-      stage("head_gemm", [&] { gemm(xn, M, h.inW, out_qkv, epi_store(qkv_mode, h.inB, ACT_NONE)); });
+      stage("head_gemm", [&] { gemm(xn, M, h.inW, out_qkv, qkv, 0, epi_store(qkv_mode, h.inB, ACT_NONE)); });
       if (!last) {
         stage("head_attn", [&] { attend_rows(items, L.items_cap, items128, L.items128_cap, soff, slen, 0); });
-        stage("head_gemm", [&] { gemm(ao, M, h.outW, out_x, epi_resid(h.outB)); });
+        stage("head_gemm", [&] { gemm(ao, M, h.outW, out_x, x, 0, epi_resid(h.outB)); });
         stage("head_ln", [&] {
           LnArgs a = ln_base(M);
           a.eps = 1e-5f;
@@ -723,8 +721,8 @@ class Replica {
           a.out_plane = xn.plane;
           launched(ln_launch(a, st));
         });
-        stage("head_gemm", [&] { gemm(xn, M, h.l1W, out_ff, epi_store(act_mode(), h.l1B, ACT_RELU)); });
-        stage("head_gemm", [&] { gemm(ff, M, h.l2W, out_x, epi_resid(h.l2B)); });
+        stage("head_gemm", [&] { gemm(xn, M, h.l1W, out_ff, ff.p, ff.plane, epi_store(act_mode(), h.l1B, ACT_RELU)); });
+        stage("head_gemm", [&] { gemm(ff, M, h.l2W, out_x, x, 0, epi_resid(h.l2B)); });
         stage("head_ln", [&] {
           LnArgs a = ln_base(M);
           a.eps = 1e-5f;
@@ -747,7 +745,7 @@ class Replica {
           a.out_f32 = xg;
           launched(ln_launch(a, st));
         });
-        stage("head_gemm", [&] { gemm(aog, R, h.outW, out_xg, epi_resid(h.outB)); });
+        stage("head_gemm", [&] { gemm(aog, R, h.outW, out_xg, xg, 0, epi_resid(h.outB)); });
         stage("head_ln", [&] {
           LnArgs a = ln_base(R);
           a.eps = 1e-5f;
@@ -758,8 +756,8 @@ class Replica {
           a.out_plane = xng.plane;
           launched(ln_launch(a, st));
         });
-        stage("head_gemm", [&] { gemm(xng, R, h.l1W, out_ffg, epi_store(act_mode(), h.l1B, ACT_RELU)); });
-        stage("head_gemm", [&] { gemm(ffg, R, h.l2W, out_xg, epi_resid(h.l2B)); });
+        stage("head_gemm", [&] { gemm(xng, R, h.l1W, out_ffg, ffg.p, ffg.plane, epi_store(act_mode(), h.l1B, ACT_RELU)); });
+        stage("head_gemm", [&] { gemm(ffg, R, h.l2W, out_xg, xg, 0, epi_resid(h.l2B)); });
         snprintf(nb, sizeof nb, "head%d", j);
         dump(nb, xg, R);
       }
@@ -773,7 +771,7 @@ class Replica {
       a.out_bf = xs.p;
       a.out_plane = xs.plane;
       launched(ln_launch(a, st));
-      gemm(xs, KT, sc1, out_hs, epi_store(P == 2 ? OUT_F32 : OUT_BF16, sc1B, ACT_GELU));
+      gemm(xs, KT, sc1, out_hs, hs, 0, epi_store(P == 2 ? OUT_F32 : OUT_BF16, sc1B, ACT_GELU));
     });
     stage("head_out", [&] {
       HeadOutArgs a;
@@ -855,9 +853,7 @@ class Replica {
         int zero = 0;
         cudaMemcpy(d_err, &zero, 4, cudaMemcpyHostToDevice);
         *herr = 0;
-        // an aborted split-K launch can leave tile counters part-way: clear them for the next pass
-        if (counters) cudaMemset(counters, 0, n_counters * 4);
-        // and an aborted attention launch its work / exit counters
+        // an aborted attention launch can leave its work / exit counters part-way: clear them
         if (d_attn_ticket) cudaMemset(d_attn_ticket, 0, 16);
       }
       (void)cudaGetLastError();

@@ -356,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int acc = local & 1;
       const uint32_t accph = (local >> 1) & 1;
       const int mb = t / num_n, nb = t - (t / num_n) * num_n;
-      const int row0 = mb * kBM + q * 32, row = row0 + lane;
+      const int row0 = mb * kBM + q * 32;
       if (!mbar_wait(smem_u32(&S.accf[acc]), accph, abort, err, kErrGemmAccFull)) break;
       tc_fence_after();
       const uint32_t tbase = tmem + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
@@ -364,69 +364,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         epilogue_tile<BN, EPI>([&](int off, float (&v)[32]) { tmem_ld32(tbase + off, v); }, row0, lane, nb, sh, ep,
                                &tc, stager);
       } else {
-        // Split-K: publish this slice's fp32 partial rows, then the warp that completes the set of
-        // slices for these 32 rows sums all of them in slice order and runs the epilogue. No CTA
-        // waits for another, and the sum does not depend on which slice finished last.
-        // Both directions go through the warp's swizzled staging tile so that global traffic is
-        // coalesced: lane l moves 16 bytes (float4 l%8) of rows l/8 + 4k.
+        // Split-K: this slice's fp32 partial tile into plane `sp` of the workspace (TMA stores of
+        // the staged 32 x 32 chunks; `tc` maps the workspace here). splitk_reduce_kernel then sums
+        // the planes in slice order and runs the epilogue, so no CTA waits for another and the
+        // result does not depend on which slice finished first.
         const int cols = min(BN, sh.N - nb * BN);
-        const int f = lane & 7, jr = lane >> 3;
-        const size_t slice = (size_t)sh.M * sh.N;
         for (int c = 0; c < cols; c += 32) {
           float v[32];
           __syncwarp();
           tmem_ld32(tbase + c, v);
           uint8_t* tile = stg_acquire(stager, lane);
           put_f32_row(tile, lane, v);
-          __syncwarp();
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int r = 4 * k + jr;
-            if (row0 + r < sh.M)
-              __stcg(reinterpret_cast<float4*>(sh.ws + sp * slice + (size_t)(row0 + r) * sh.N + nb * BN + c) + f,
-                     *reinterpret_cast<const float4*>(tile + r * 128 + ((f ^ (r & 7)) << 4)));
-          }
-        }
-        __syncwarp();
-        __threadfence();
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) last = atomicAdd(sh.counters + (size_t)t * 4 + q, 1) == splits - 1;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-          __threadfence();
-          if (lane == 0) sh.counters[(size_t)t * 4 + q] = 0;  // ready for the next launch
-          epilogue_tile<BN, EPI>(
-              [&](int off, float (&v)[32]) {
-                // sum of every slice, 16-byte pieces loaded coalesced (all slices of a piece in
-                // flight together, summed in slice order), then transposed to one row per thread
-                uint8_t* tile = stg_acquire(stager, lane);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                  const int r = 4 * k + jr;
-                  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                  if (row0 + r < sh.M) {
-                    const float4* src =
-                        reinterpret_cast<const float4*>(sh.ws + (size_t)(row0 + r) * sh.N + nb * BN + off) + f;
-                    float4 p[kMaxSplits];
-#pragma unroll
-                    for (int s2 = 0; s2 < kMaxSplits; ++s2)
-                      if (s2 < splits) p[s2] = __ldcg(src + s2 * (slice / 4));
-#pragma unroll
-                    for (int s2 = 0; s2 < kMaxSplits; ++s2)
-                      if (s2 < splits) { acc.x += p[s2].x; acc.y += p[s2].y; acc.z += p[s2].z; acc.w += p[s2].w; }
-                  }
-                  *reinterpret_cast<float4*>(tile + r * 128 + ((f ^ (r & 7)) << 4)) = acc;
-                }
-                __syncwarp();
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  const float4 q4 = *reinterpret_cast<const float4*>(tile + lane * 128 + ((j ^ (lane & 7)) << 4));
-                  v[4 * j] = q4.x; v[4 * j + 1] = q4.y; v[4 * j + 2] = q4.z; v[4 * j + 3] = q4.w;
-                }
-                __syncwarp();
-              },
-              row0, lane, nb, sh, ep, &tc, stager);
+          stg_issue(stager, lane, &tc, nb * BN + c, row0, sp, false);
         }
       }
       tc_fence_before();
@@ -444,6 +393,93 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 2 * BN);
+  }
+}
+
+// ------------------------------------------------------------------ split-K epilogue
+// out = epilogue(sum over slices s of ws[s]) for rows < M, the slices summed in order. One thread per
+// (row, 64-column output block, t = 0..7): output columns 4t..4t+3 and 32+4t..35+4t of the block (a
+// RoPE rotation pairs column i with i + 32), or for GeGLU the block's outputs 8t..8t+7, whose input
+// and gate sums sit at accumulator columns 128*blk + 8t.. and 128*blk + 64 + 8t.. (interleaved B).
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+  return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+
+// Four consecutive output columns of one row in the epilogue's output format.
+__device__ __forceinline__ void put4(const GemmShape& sh, const GemmEpi& ep, long long row, int ncols, int col,
+                                     float4 v) {
+  const long long at = row * ncols + col;
+  if (ep.out_mode == OUT_F32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(sh.dst) + at) = v;
+    return;
+  }
+  bf16* o = static_cast<bf16*>(sh.dst);
+  const uint32_t h0 = pack_bf16x2(v.x, v.y), h1 = pack_bf16x2(v.z, v.w);
+  *reinterpret_cast<uint2*>(o + at) = make_uint2(h0, h1);
+  if (ep.out_mode == OUT_BF16X2) {
+    const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h0));
+    const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h1));
+    *reinterpret_cast<uint2*>(o + sh.dst_plane + at) =
+        make_uint2(pack_bf16x2(v.x - f0.x, v.y - f0.y), pack_bf16x2(v.z - f1.x, v.w - f1.y));
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmShape sh, const GemmEpi ep) {
+  pdl_trigger();
+  pdl_wait();
+  const int ncols = EPI == EPI_GEGLU ? ep.geglu_I : sh.N;
+  const int per_row = (ncols / 64) * 8;
+  const long long gid = static_cast<long long>(blockIdx.x) * 256 + threadIdx.x;
+  const long long row = gid / per_row;
+  if (row >= sh.M) return;
+  const int rem = static_cast<int>(gid - row * per_row), blk = rem >> 3, t = rem & 7;
+  const size_t plane = static_cast<size_t>(sh.M) * sh.N;
+  const float* ws = sh.ws + static_cast<size_t>(row) * sh.N;
+  auto sum4 = [&](int col) {
+    float4 a = __ldcg(reinterpret_cast<const float4*>(ws + col));
+    for (int s = 1; s < sh.splits; ++s) a = add4(a, __ldcg(reinterpret_cast<const float4*>(ws + s * plane + col)));
+    return a;
+  };
+  if constexpr (EPI == EPI_GEGLU) {
+    const int in = 128 * blk + 8 * t, out = 64 * blk + 8 * t;
+    const float4 x0 = sum4(in), x1 = sum4(in + 4), g0 = sum4(in + 64), g1 = sum4(in + 68);
+    put4(sh, ep, row, ncols, out,
+         make_float4(gelu_as(x0.x) * g0.x, gelu_as(x0.y) * g0.y, gelu_as(x0.z) * g0.z, gelu_as(x0.w) * g0.w));
+    put4(sh, ep, row, ncols, out + 4,
+         make_float4(gelu_as(x1.x) * g1.x, gelu_as(x1.y) * g1.y, gelu_as(x1.z) * g1.z, gelu_as(x1.w) * g1.w));
+  } else {
+    const int c0 = 64 * blk + 4 * t, c1 = c0 + 32;
+    float4 a = sum4(c0), b = sum4(c1);
+    if (ep.bias) {
+      a = add4(a, *reinterpret_cast<const float4*>(ep.bias + c0));
+      b = add4(b, *reinterpret_cast<const float4*>(ep.bias + c1));
+    }
+    if constexpr (EPI == EPI_RESID) {
+      float4* x0 = reinterpret_cast<float4*>(static_cast<float*>(sh.dst) + row * sh.N + c0);
+      float4* x1 = reinterpret_cast<float4*>(static_cast<float*>(sh.dst) + row * sh.N + c1);
+      *x0 = add4(*x0, a);
+      *x1 = add4(*x1, b);
+      return;
+    }
+    if constexpr (EPI == EPI_ROPE) {
+      if (c0 < ep.rope_cols) {
+        const long long p = ep.pos[row];
+        const float4 cs = *reinterpret_cast<const float4*>(ep.cos_t + p * 32 + 4 * t);
+        const float4 sn = *reinterpret_cast<const float4*>(ep.sin_t + p * 32 + 4 * t);
+        const float4 ra = make_float4(a.x * cs.x - b.x * sn.x, a.y * cs.y - b.y * sn.y, a.z * cs.z - b.z * sn.z,
+                                      a.w * cs.w - b.w * sn.w);
+        const float4 rb = make_float4(b.x * cs.x + a.x * sn.x, b.y * cs.y + a.y * sn.y, b.z * cs.z + a.z * sn.z,
+                                      b.w * cs.w + a.w * sn.w);
+        a = ra;
+        b = rb;
+      }
+    } else if (ep.act != ACT_NONE) {
+      a = make_float4(apply_act(a.x, ep.act), apply_act(a.y, ep.act), apply_act(a.z, ep.act), apply_act(a.w, ep.act));
+      b = make_float4(apply_act(b.x, ep.act), apply_act(b.y, ep.act), apply_act(b.z, ep.act), apply_act(b.w, ep.act));
+    }
+    put4(sh, ep, row, ncols, c0, a);
+    put4(sh, ep, row, ncols, c1, b);
   }
 }
 
@@ -636,8 +672,17 @@ cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   const int work = ((sh.M + kBM - 1) / kBM) * ((sh.N + BN - 1) / BN) * (sh.splits > 1 ? sh.splits : 1);
   const int grid = work < grid_ctas ? work : grid_ctas;
   if (grid <= 0) return cudaSuccess;
-  if (sh.splits > 1)
-    return launch_pdl(gemm_tc_kernel<BN, EPI, true>, dim3(grid), dim3(kThreads), smem, st, ta, tb, tc, sh, ep, err);
+  if (sh.splits > 1) {
+    CUtensorMap tp;  // the workspace [splits][M][N] fp32, the target of the slices' partial tiles
+    if (!make_output_map(&tp, sh.ws, true, (uint64_t)sh.N, (uint64_t)sh.M, (uint64_t)sh.splits))
+      return cudaErrorInvalidValue;
+    cudaError_t e =
+        launch_pdl(gemm_tc_kernel<BN, EPI, true>, dim3(grid), dim3(kThreads), smem, st, ta, tb, tp, sh, ep, err);
+    if (e != cudaSuccess) return e;
+    const int ncols = EPI == EPI_GEGLU ? ep.geglu_I : sh.N;
+    const long long threads = (long long)sh.M * (ncols / 64) * 8;
+    return launch_pdl(splitk_reduce_kernel<EPI>, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, st, sh, ep);
+  }
   return launch_pdl(gemm_tc_kernel<BN, EPI, false>, dim3(grid), dim3(kThreads), smem, st, ta, tb, tc, sh, ep, err);
 }
 
@@ -740,7 +785,10 @@ cudaError_t gemm_prepare_device() {
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, int bn,
                         const GemmShape& sh, const GemmEpi& ep, int* err, int grid_ctas, cudaStream_t st) {
   if (sh.M <= 0) return cudaSuccess;
-  if (sh.splits > 1 && (bn == kGemmPair || !sh.ws || !sh.counters || sh.splits > kMaxSplits)) return cudaErrorInvalidValue;
+  if (sh.splits > 1 && (bn == kGemmPair || !sh.ws || !sh.dst || sh.splits > kMaxSplits ||
+                        (reinterpret_cast<uintptr_t>(sh.ws) & 15) != 0 || (reinterpret_cast<uintptr_t>(sh.dst) & 15) != 0 ||
+                        (ep.out_mode == OUT_BF16X2 && ep.kind != EPI_RESID && sh.dst_plane % 4 != 0)))
+    return cudaErrorInvalidValue;
   if (sh.N % 64 != 0 || sh.K % 8 != 0 || (sh.nseg != 1 && sh.nseg != 3)) return cudaErrorInvalidValue;
   if (ep.kind == EPI_GEGLU && (ep.geglu_I % 64 != 0 || sh.N != 2 * ep.geglu_I)) return cudaErrorInvalidValue;
   if (ep.kind == EPI_ROPE && (ep.rope_cols % 64 != 0 || !ep.pos || !ep.cos_t || !ep.sin_t))

@@ -25,31 +25,34 @@ struct GemmShape {
   int K;     // reduction length of one segment
   int nseg;  // 1 (bf16) or 3 (split-bf16 fp32 emulation)
   // Split-K (single-CTA tiles only): the K loop is cut into `splits` slices run by different CTAs.
-  // Each slice writes its fp32 partial to ws[splits][M][N]; the last slice to finish sums them in
-  // slice order and runs the epilogue. counters: one int per (128-row tile, 32-row quarter), zero
-  // before the first launch and left zero by every completed launch.
+  // Slice s stores its fp32 partial tile into plane s of ws[splits][M][N] (16-byte aligned); a second
+  // kernel sums the planes in slice order and runs the epilogue into `dst`, the buffer the output map
+  // covers (x [M][N] fp32 for EPI_RESID, else [planes][M][cols] in the output format, planes
+  // `dst_plane` elements apart).
   int splits = 1;
   float* ws = nullptr;
-  int* counters = nullptr;
+  void* dst = nullptr;
+  long long dst_plane = 0;
 };
 constexpr int kMaxSplits = 8;
-// Workspace floats and counter ints a split-K launch needs.
+// Workspace floats a split-K launch needs.
 inline size_t splitk_ws_floats(int M, int N, int splits) { return (size_t)splits * M * N; }
-inline size_t splitk_counters(int M, int N, int bn) {
-  return (size_t)((M + 127) / 128) * ((N + bn - 1) / bn) * 4;
-}
-// Slice count that best fills `sms` SMs with `tiles` output tiles and `kblocks` 64-wide K blocks:
-// the smallest S minimising waves(tiles * S) / S, with at least 4 K blocks per slice; 1 when the
-// tiles already fill the GPU.
+// Slice count for `tiles` 128 x 128 output tiles of `kblocks` 64-wide K blocks on `sms` SMs: the S
+// minimising waves(tiles * S) * ceil(kblocks / S) + (S > 1 ? kSplitReduceBlocks : 0), i.e. the main
+// loop in K-block times plus the partials' round trip through memory and the reduce kernel, which
+// measured about 28 K-block times (11 us) on B200 at 512 rows. At least 4 K blocks per slice; 1 when
+// the tiles already fill the GPU. At 512 rows this splits the long-K GEMMs (MLP-out, K = 2624; the
+// head's FFN-2, K = 4096) and keeps whole-K tiles for K = 1024.
+constexpr int kSplitReduceBlocks = 28;
 inline int splitk_choose(int tiles, int kblocks, int sms) {
   if (tiles >= sms) return 1;
   int best = 1;
-  double best_cost = 1e30;
-  for (int s = 1; s <= kMaxSplits; ++s) {
-    if (s > 1 && kblocks / s < 4) break;
-    const int waves = (tiles * s + sms - 1) / sms;
-    const double cost = (double)waves / s * (1.0 + 0.15 * (s - 1));  // each slice adds partial traffic
-    if (cost < best_cost - 1e-9) { best_cost = cost; best = s; }
+  long long best_cost = kblocks;
+  for (int s = 2; s <= kMaxSplits; ++s) {
+    if (kblocks / s < 4) break;
+    const long long waves = (tiles * s + sms - 1) / sms;
+    const long long cost = waves * ((kblocks + s - 1) / s) + kSplitReduceBlocks;
+    if (cost < best_cost) { best_cost = cost; best = s; }
   }
   return best;
 }
