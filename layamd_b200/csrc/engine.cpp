@@ -519,8 +519,13 @@ class Replica {
     if (W.N < 256) return 128;
     const long long tp = (long long)((M + 255) / 256) * ((W.N + 255) / 256);
     if (pair_clusters > 0 && tp >= 2LL * pair_clusters) return kGemmPair;
-    const long long t256 = (long long)((M + 127) / 128) * ((W.N + 255) / 256);
-    return t256 >= 2LL * num_sms ? 256 : 128;
+    // whole waves of 128 x 128 against 128 x 256 tiles; a 128 x 256 tile costs about 1.6 of the
+    // narrow one (it reads each A block once per 256 columns): at 512 rows the GeGLU GEMM runs one
+    // wave of 84 wide tiles in 13 us against two waves of 164 narrow ones in 17 us
+    const long long rows = (M + 127) / 128;
+    const long long w128 = (rows * ((W.N + 127) / 128) + num_sms - 1) / num_sms;
+    const long long w256 = (rows * ((W.N + 255) / 256) + num_sms - 1) / num_sms;
+    return 10 * w128 > 16 * w256 ? 256 : 128;
   }
   // out: the epilogue's output map; dst / dst_plane: the buffer it covers (for a split-K launch,
   // whose epilogue runs in a second kernel on plain pointers).

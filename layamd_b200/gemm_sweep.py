@@ -34,10 +34,16 @@ def peaks():
 
 def pick_tile(M, N, sms):
     """The engine's rule (engine.cpp Replica::pick_tile): the CTA-pair 256 x 256 tile when its tiles
-    fill every co-resident pair twice, else 128 x 256 when those fill every SM twice, else 128 x 128."""
+    fill every co-resident pair twice, else the width with fewer whole waves, a 128 x 256 tile
+    counting 1.6 of a 128 x 128 one."""
+    if N < 256:
+        return 128
     if ((M + 255) // 256) * ((N + 255) // 256) >= 2 * (sms // 2):
         return 512
-    return 256 if ((M + 127) // 128) * ((N + 255) // 256) >= 2 * sms else 128
+    rows = (M + 127) // 128
+    w128 = (rows * ((N + 127) // 128) + sms - 1) // sms
+    w256 = (rows * ((N + 255) // 256) + sms - 1) // sms
+    return 256 if 10 * w128 > 16 * w256 else 128
 
 
 def interleave_geglu(W, I):
