@@ -33,8 +33,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from oracle import workloads  # noqa: E402  (input generator only)
-from oracle import synth  # noqa: E402  (seeded checkpoint files)
+from layamd_b200.synthetic import workloads  # noqa: E402  (input generator only)
+from layamd_b200.synthetic import synth  # noqa: E402  (seeded checkpoint files)
 
 METRIC = "decisions/sec at ModernBERT-large seq512, 1/2/4/8 B200; p50 batch-1 latency"
 WORKLOAD = ("C2: ModernBERT-large (28 layers, d1024, GeGLU 2624, window 128) bf16 weights / fp32 accumulation; "

@@ -30,7 +30,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 from layamd_b200 import server as S  # noqa: E402
-from oracle import synth  # noqa: E402  (seeded checkpoint and tokenizer files only)
+from layamd_b200.synthetic import synth  # noqa: E402  (seeded checkpoint and tokenizer files only)
 
 
 def make_requests(n_states=64, seed=1):

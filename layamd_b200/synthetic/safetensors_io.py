@@ -1,4 +1,4 @@
-"""Minimal safetensors container I/O with numpy (test infrastructure; see oracle/__init__.py).
+"""Minimal safetensors container I/O with numpy, for writing and reading the synthetic checkpoints.
 
 Format: 8-byte little-endian header length, a JSON header mapping tensor names to
 {dtype, shape, data_offsets}, then the raw little-endian tensor bytes. The engine's C++ loader reads

@@ -1,5 +1,5 @@
-"""Seeded random-init Laya checkpoints in the reference's on-disk layout (test infrastructure; see
-oracle/__init__.py).
+"""Seeded random-init Laya checkpoints in the reference's on-disk layout, for the tests and the
+benchmarks (no real checkpoint is available to them).
 
 A checkpoint directory holds what the reference engine loads (src/engine.hip:140-176,
 src/laya.cpp:5-41): ``model.safetensors`` with the reference tensor names, ``encoder/config.json``

@@ -1,5 +1,5 @@
-"""Seeded synthetic inputs of the benchmark configurations (test infrastructure; also imported by
-bench.py to build its inputs -- the token generator only, no oracle compute).
+"""Seeded synthetic inputs of the benchmark configurations, for the tests and the benchmarks (token
+ids and option markers only; nothing here computes the model).
 
 Every question is a dict {ids, markers, qtype} in the reference ABI's terms
 (src/laya_api.h:6-9): token ids of one sequence, option-marker positions within it, question type

@@ -8,7 +8,7 @@ C3: mmBERT-base architecture (22 layers, d768, 12 heads, GeGLU 1152, vocab 25600
 C4: ModernBERT-large architecture at max_len 1024, B=256 sequences with L log-uniform in [128,1024],
     question types cycling choice / score / yes-no with 2-6 options.
 Weights are the seeded random-init checkpoints (N(0,0.02), seed 0) served in bf16; inputs are the
-seeded synthetic batches of oracle/workloads.py. One handle over the listed GPUs shards every call's
+seeded synthetic batches of layamd_b200/synthetic/workloads.py. One handle over the listed GPUs shards every call's
 questions across them (no collective).
 
 Reported: `value` decisions/s with the packed inputs resident in HBM (laya_stage + laya_replay: CUDA
@@ -29,7 +29,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-from oracle import synth, workloads  # noqa: E402  (checkpoint generator and input batches only)
+from layamd_b200.synthetic import synth, workloads  # noqa: E402  (checkpoint generator and input batches only)
 from layamd_b200 import load_lib  # noqa: E402
 
 CONFIGS = {

@@ -5,11 +5,11 @@ Nothing in the engine (``layamd_b200``) imports, links or calls this package. On
 use it, and only as the checker or the timed CPU baseline, never as a compute path of the product.
 
 Contents:
-  safetensors_io  minimal reader/writer of the safetensors container (numpy)
-  synth           seeded random-init checkpoints of the benchmark architectures
   model           numpy fp32 restatement of the reference forward pass (ref/rl_common.py
                   DecisionModel + transformers ModernBertModel), per-layer capture included
-  workloads       the seeded synthetic inputs of the benchmark configurations
+
+The seeded checkpoints and inputs it is run on come from ``layamd_b200.synthetic`` (input
+generators, shared with the benchmarks; they compute nothing of the model).
 
 Parity pin: ``model`` is checked against the reference's own PyTorch path (ref/rl_common.py with
 the transformers ModernBertModel encoder) run in the build container on the same synthetic

@@ -13,7 +13,7 @@ import tempfile
 import numpy as np
 
 from layamd_b200 import PRECISION_BF16, PRECISION_FP32_PARITY, load_lib  # noqa: F401
-from oracle import workloads
+from layamd_b200.synthetic import workloads
 
 IP = ctypes.POINTER(ctypes.c_int)
 FP = ctypes.POINTER(ctypes.c_float)

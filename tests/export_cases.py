@@ -7,7 +7,7 @@ import shutil
 
 import numpy as np
 
-from oracle import safetensors_io, synth
+from layamd_b200.synthetic import safetensors_io, synth
 
 CASES = ("fp16", "names", "shape", "dtype", "layout", "maxlen", "headlayers", "several")
 

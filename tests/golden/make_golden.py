@@ -7,7 +7,7 @@ which only read the committed .npz files):
     python tests/golden/make_golden.py
 
 What it does, following ref/gen_golden.py:51-105 of the reference:
-  1. builds each synthetic checkpoint with oracle.synth (seeded init rule) and checks that the
+  1. builds each synthetic checkpoint with layamd_b200.synthetic.synth (seeded init rule) and checks that the
      reference DecisionModel (ref/rl_common.py:127-134 build_model, attn_implementation="sdpa") has
      exactly the tensor names, order and shapes the generator writes, then loads it strict=True;
   2. runs the model in fp32 on CPU on each case as ONE padded batch (collate_items,
@@ -25,7 +25,7 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 sys.path.insert(0, ROOT)
-from oracle import synth, workloads  # noqa: E402
+from layamd_b200.synthetic import synth, workloads  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF = os.environ.get("LAYA_REFERENCE", "/root/reference")
@@ -50,7 +50,7 @@ def reference_model(ckpt):
     sd = model.state_dict()
     specs = synth.param_specs(synth.load_arch(ckpt))
     names = [n for n, _, _ in specs]
-    assert list(sd.keys()) == names, "state_dict order differs from oracle.synth.param_specs"
+    assert list(sd.keys()) == names, "state_dict order differs from layamd_b200.synthetic.synth.param_specs"
     for n, shape, _ in specs:
         assert tuple(sd[n].shape) == tuple(shape), (n, sd[n].shape, shape)
     w = synth.load_weights(ckpt)

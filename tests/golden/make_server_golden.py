@@ -8,7 +8,7 @@ Run in the build container, where the reference checkout is available (LAYA_REFE
 It imports the reference's server/laya_server.py in place and drives ``Laya.prepare`` and
 ``Laya.finish`` (server/laya_server.py:143-188) on an instance built without its engine (only
 ``max_markers`` of the engine is read by those two methods), with the synthetic word-level tokenizer
-of the tiny checkpoint (oracle/synth.py ``write_tokenizer``), over requests chosen to reach every
+of the tiny checkpoint (layamd_b200/synthetic/synth.py ``write_tokenizer``), over requests chosen to reach every
 branch of the sequence construction (server/laya_server.py:82-107): list / dict / described choice
 criteria, score levels, yes/no with and without custom wording, JSON states and instructions,
 [MASK] inside texts, states longer than max_len, many options (per-option truncation), options that
@@ -26,7 +26,7 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 sys.path.insert(0, ROOT)
-from oracle import synth  # noqa: E402
+from layamd_b200.synthetic import synth  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF = os.environ.get("LAYA_REFERENCE", "/root/reference")

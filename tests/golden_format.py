@@ -8,7 +8,7 @@ import os
 import numpy as np
 
 from oracle import model as om
-from oracle import synth
+from layamd_b200.synthetic import synth
 
 QT = ("choice", "score", "noul")
 

@@ -16,7 +16,7 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 from oracle import model as om  # noqa: E402
-from oracle import synth, workloads  # noqa: E402
+from layamd_b200.synthetic import synth, workloads  # noqa: E402
 from tests.engine_helpers import (Handle, act_rel, argmax_agree, gathered_rows, prob_delta, read_dump,  # noqa: E402
                                   rel)
 

@@ -8,7 +8,7 @@ import pytest
 torch = pytest.importorskip("torch")
 
 from oracle import model as om  # noqa: E402
-from oracle import synth, workloads  # noqa: E402
+from layamd_b200.synthetic import synth, workloads  # noqa: E402
 from tests import export_cases  # noqa: E402
 from tests.engine_helpers import Handle, act_rel, prob_delta  # noqa: E402
 

@@ -6,7 +6,7 @@ import os
 import numpy as np
 
 from layamd_b200 import golden_parity as G
-from oracle import synth
+from layamd_b200.synthetic import synth
 from tests import golden_format
 
 

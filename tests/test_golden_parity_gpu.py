@@ -9,7 +9,7 @@ import pytest
 torch = pytest.importorskip("torch")
 
 from layamd_b200 import golden_parity as G  # noqa: E402
-from oracle import synth  # noqa: E402
+from layamd_b200.synthetic import synth  # noqa: E402
 from tests import golden_format  # noqa: E402
 
 pytestmark = pytest.mark.gpu

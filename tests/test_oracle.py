@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 
 from oracle import model as om
-from oracle import synth
+from layamd_b200.synthetic import synth
 
 GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 

@@ -11,7 +11,7 @@ torch = pytest.importorskip("torch")
 
 from layamd_b200 import server as S  # noqa: E402
 from oracle import model as om  # noqa: E402
-from oracle import synth  # noqa: E402
+from layamd_b200.synthetic import synth  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
