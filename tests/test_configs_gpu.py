@@ -1,0 +1,74 @@
+"""Parity at the other two benchmark configurations, against the oracle on the same seeded
+checkpoints: mmBERT-base (C3: d 768, 12 heads, 22 layers, GeGLU 1152, vocabulary 256000, pad id 0,
+context 1024) and ModernBERT-large at context 1024 (C4: sequences past 512 tokens, RoPE positions
+and global attention up to 1024 keys), in fp32-parity and bf16 mode."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from layamd_b200.synthetic import synth, workloads  # noqa: E402
+from oracle import model as om  # noqa: E402
+from tests.engine_helpers import Handle, act_rel, argmax_agree, gathered_rows, prob_delta, read_dump, rel  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+ENV = {"LAYA_MAX_TOKENS": 16384}
+
+
+@pytest.fixture(scope="module", autouse=True)
+def need_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def spread(qs, n):
+    """n questions spread over the batch's lengths, the longest included."""
+    order = sorted(range(len(qs)), key=lambda i: len(qs[i]["ids"]))
+    picks = sorted({order[int(round(j * (len(order) - 1) / (n - 1)))] for j in range(n)})
+    return [qs[i] for i in picks]
+
+
+def check_both_modes(ckpt, qs, oracle):
+    lo_o, ac_o, _ = oracle.forward_batch(qs)
+    for precision, dp, da in ((1, 1e-4, 1e-3), (0, 0.01, 0.05)):
+        h = Handle(ckpt, precision, env=ENV)
+        try:
+            rc, lo, ac = h.forward(qs)
+        finally:
+            h.close()
+        assert rc == 0
+        assert prob_delta(lo, lo_o, qs) <= dp, precision
+        assert act_rel(ac, ac_o) <= da, precision
+        if precision == 0:
+            assert argmax_agree(lo, lo_o, qs)
+
+
+def test_mmbert_base_c3_shapes():
+    ck = synth.checkpoint("base", 0)
+    o = om.Oracle(synth.load_weights(ck), synth.load_arch(ck))
+    qs = spread(workloads.c3(synth.ARCHS["base"]), 6)
+    assert max(len(q["ids"]) for q in qs) > 900
+    check_both_modes(ck, qs, o)
+
+
+def test_large_context_1024_c4_shapes():
+    ck = synth.checkpoint("large1024", 0)
+    a = synth.load_arch(ck)
+    o = om.Oracle(synth.load_weights(ck), a)
+    qs = spread(workloads.c4(synth.ARCHS["large1024"]), 6)
+    assert max(len(q["ids"]) for q in qs) > 1000
+    check_both_modes(ck, qs, o)
+    # every hidden state of the longest question in fp32-parity mode (max |a - b| / max |b| <= 1e-3)
+    q = [max(qs, key=lambda x: len(x["ids"]))]
+    h = Handle(ck, 1, env=ENV)
+    try:
+        lo, ac, d = h.forward_dump(q)
+    finally:
+        h.close()
+    _, _, caps = o.forward_batch(q, capture=True)
+    worst = {k: rel(read_dump(d, k, a.d), caps[0][k])
+             for k in ["emb"] + ["enc%d" % i for i in range(a.layers)] + ["final", "head0"]}
+    worst["head1"] = rel(read_dump(d, "head1", a.d), gathered_rows("head1", q, caps))
+    bad = {k: v for k, v in worst.items() if v > 1e-3}
+    assert not bad, bad
+    assert np.isfinite(lo).all()
