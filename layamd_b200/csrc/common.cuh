@@ -359,6 +359,60 @@ __device__ __forceinline__ uint64_t sdesc_mn128(uint32_t saddr) {
   return d;
 }
 
+// ---- one row of D = 128*NV fp32 values per warp, lane holding columns 4*(lane + 32*i) .. +3 ----
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// In place: v = (v - mean) / sqrt(var + eps) * w (+ b), mean and variance two-pass in fp32 over the
+// warp's row (torch.nn.LayerNorm's definition). Every LayerNorm of the engine goes through this one
+// routine, so a fused and a separate LayerNorm of the same row give the same bits.
+template <int NV>
+__device__ __forceinline__ void layer_norm_regs(float4 (&v)[NV], const float* w, const float* b, float eps, int D,
+                                                int lane) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  const float mean = warp_sum(s) / D;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    v[i].x -= mean; v[i].y -= mean; v[i].z -= mean; v[i].w -= mean;
+    q += (v[i].x * v[i].x + v[i].y * v[i].y) + (v[i].z * v[i].z + v[i].w * v[i].w);
+  }
+  const float rstd = 1.f / sqrtf(warp_sum(q) / D + eps);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float4 g = reinterpret_cast<const float4*>(w)[lane + 32 * i];
+    float4 r = make_float4(v[i].x * rstd * g.x, v[i].y * rstd * g.y, v[i].z * rstd * g.z, v[i].w * rstd * g.w);
+    if (b) {
+      const float4 bb = reinterpret_cast<const float4*>(b)[lane + 32 * i];
+      r.x += bb.x; r.y += bb.y; r.z += bb.z; r.w += bb.w;
+    }
+    v[i] = r;
+  }
+}
+
+// The row as bf16 (hi) and, with two planes, the bf16 rounding of what the hi plane missed (lo).
+template <int NV>
+__device__ __forceinline__ void store_bf16_planes(const float4 (&v)[NV], __nv_bfloat16* hi_row, __nv_bfloat16* lo_row,
+                                                  int planes, int lane) {
+  uint2* hi = reinterpret_cast<uint2*>(hi_row);
+  uint2* lo = reinterpret_cast<uint2*>(lo_row);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const uint32_t h0 = pack_bf16x2(v[i].x, v[i].y), h1 = pack_bf16x2(v[i].z, v[i].w);
+    hi[lane + 32 * i] = make_uint2(h0, h1);
+    if (planes == 2) {
+      const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h0));
+      const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h1));
+      lo[lane + 32 * i] = make_uint2(pack_bf16x2(v[i].x - f0.x, v[i].y - f0.y), pack_bf16x2(v[i].z - f1.x, v[i].w - f1.y));
+    }
+  }
+}
+
 // Instruction descriptor: bf16 x bf16 -> fp32, both operands K-major, M x N tile.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4)      // D format fp32

@@ -123,6 +123,7 @@ class Replica {
   float* ws = nullptr;
   size_t ws_floats = 0;
   bool use_splitk = true;
+  bool split_ln = true;  // LAYA_SPLIT_LN=0: a split-K residual GEMM leaves its LayerNorm to the LN kernel
   cudaStream_t st = nullptr;
   std::vector<void*> allocs;
   std::vector<void*> host_allocs;
@@ -392,6 +393,7 @@ class Replica {
     // GPU (a few thousand rows at most: batch-1 and small calls), its K loop is cut into slices
     // whose partials a second kernel sums in order. 32 M floats (128 MB) cover every split count.
     use_splitk = !(getenv("LAYA_SPLITK") && atoi(getenv("LAYA_SPLITK")) == 0);
+    split_ln = !(getenv("LAYA_SPLIT_LN") && atoi(getenv("LAYA_SPLIT_LN")) == 0);
     if (use_splitk) {
       ws_floats = (size_t)32 << 20;
       if (!dalloc(&ws, ws_floats * 4, err)) return false;
@@ -528,11 +530,14 @@ class Replica {
     return 10 * w128 > 16 * w256 ? 256 : 128;
   }
   // out: the epilogue's output map; dst / dst_plane: the buffer it covers (for a split-K launch,
-  // whose epilogue runs in a second kernel on plain pointers).
-  void gemm(const Operand& A, int M, const Mat& W, const CUtensorMap& out, void* dst, long long dst_plane,
-            const GemmEpi& ep) {
+  // whose epilogue runs in a second kernel on plain pointers). ln_w: for a residual GEMM, the gain of
+  // the LayerNorm that follows it into xn; when the GEMM runs split-K, its reduce kernel writes that
+  // LayerNorm too and gemm() returns true (the caller then skips its LayerNorm launch).
+  bool gemm(const Operand& A, int M, const Mat& W, const CUtensorMap& out, void* dst, long long dst_plane,
+            GemmEpi ep, const float* ln_w = nullptr) {
     int bn = pick_tile(M, W);
     GemmShape sh{M, W.N, W.K, nseg};
+    bool ln_fused = false;
     if (bn == 128 && use_splitk) {
       // too few 128 x 128 tiles to fill the GPU: split the K loop (deterministic partial sums)
       const int tiles = ((M + 127) / 128) * ((W.N + 127) / 128);
@@ -543,9 +548,18 @@ class Replica {
         sh.ws = ws;
         sh.dst = dst;
         sh.dst_plane = dst_plane;
+        if (ln_w && split_ln && ep.kind == EPI_RESID && W.N % 256 == 0 && W.N <= 1024) {
+          ep.ln_w = ln_w;
+          ep.ln_eps = cfg.norm_eps;
+          ep.ln_out = xn.p;
+          ep.ln_plane = xn.plane;
+          ep.ln_planes = P;
+          ln_fused = true;
+        }
       }
     }
     launched(gemm_launch(A.map, bn == 256 ? W.m256 : W.m128, out, bn, sh, ep, d_err, num_sms, st));
+    return ln_fused;
   }
   GemmEpi epi_store(int out_mode, const float* bias, int act) const {
     GemmEpi e;
@@ -685,10 +699,13 @@ class Replica {
         e.geglu_I = I;
         gemm(xn, M, enc[l].Wi, out_mg, mg.p, mg.plane, e);
       });
-      stage("gemm_mlp_out", [&] { gemm(mg, M, enc[l].Wmo, out_x, x, 0, epi_resid(nullptr)); });
+      bool ln_done = false;  // the next layer's attention LayerNorm, fused into a split-K reduce
+      stage("gemm_mlp_out", [&] {
+        ln_done = gemm(mg, M, enc[l].Wmo, out_x, x, 0, epi_resid(nullptr), l + 1 < NL ? enc[l + 1].attn_norm : nullptr);
+      });
       snprintf(nb, sizeof nb, "enc%d", l);
       dump(nb, x, p.T);
-      stage("ln", [&] {
+      if (!ln_done) stage("ln", [&] {
         LnArgs a = ln_base(M);
         a.src = x;
         a.out_bf = xn.p;

@@ -483,6 +483,44 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmShape sh, 
   }
 }
 
+// Split-K residual epilogue with the following LayerNorm: one warp per row, x[row] += the slices'
+// sum (+ bias) in the same order as splitk_reduce_kernel, then ln_out[row] = LayerNorm(x[row]) * ln_w
+// through layer_norm_regs (as the LayerNorm kernel computes it).
+template <int NV>
+__global__ void __launch_bounds__(256) splitk_reduce_ln_kernel(const GemmShape sh, const GemmEpi ep) {
+  pdl_trigger();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row = static_cast<long long>(blockIdx.x) * 8 + warp;
+  if (row >= sh.M) return;
+  const size_t plane = static_cast<size_t>(sh.M) * sh.N;
+  const float4* ws = reinterpret_cast<const float4*>(sh.ws + static_cast<size_t>(row) * sh.N);
+  float4* x = reinterpret_cast<float4*>(static_cast<float*>(sh.dst) + row * sh.N);
+  // slice by slice, the lane's NV pieces of a slice (and of x with the first) in flight together
+  float4 a[NV], v[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    a[i] = __ldcg(ws + lane + 32 * i);
+    v[i] = x[lane + 32 * i];
+  }
+  for (int s = 1; s < sh.splits; ++s) {
+    float4 p[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) p[i] = __ldcg(ws + s * (plane / 4) + lane + 32 * i);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) a[i] = add4(a[i], p[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + 32 * i;
+    if (ep.bias) a[i] = add4(a[i], reinterpret_cast<const float4*>(ep.bias)[c]);
+    v[i] = add4(v[i], a[i]);
+    x[c] = v[i];
+  }
+  layer_norm_regs<NV>(v, ep.ln_w, nullptr, ep.ln_eps, sh.N, lane);
+  store_bf16_planes<NV>(v, ep.ln_out + row * sh.N, ep.ln_out + ep.ln_plane + row * sh.N, ep.ln_planes, lane);
+}
+
 // ------------------------------------------------------------------ CTA-pair variant
 // The same pipeline on a cluster of two CTAs (one per SM) computing a 256 x 256 tile with the 2-SM
 // MMA (tcgen05.mma.cta_group::2): each CTA stages its own 128 rows of A and its own 128 rows of B, so
@@ -679,6 +717,18 @@ cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     cudaError_t e =
         launch_pdl(gemm_tc_kernel<BN, EPI, true>, dim3(grid), dim3(kThreads), smem, st, ta, tb, tp, sh, ep, err);
     if (e != cudaSuccess) return e;
+    if constexpr (EPI == EPI_RESID) {
+      if (ep.ln_w) {  // the following LayerNorm in the same pass over the rows
+        const dim3 g((unsigned)((sh.M + 7) / 8));
+        switch (sh.N / 128) {
+          case 2: return launch_pdl(splitk_reduce_ln_kernel<2>, g, dim3(256), 0, st, sh, ep);
+          case 4: return launch_pdl(splitk_reduce_ln_kernel<4>, g, dim3(256), 0, st, sh, ep);
+          case 6: return launch_pdl(splitk_reduce_ln_kernel<6>, g, dim3(256), 0, st, sh, ep);
+          case 8: return launch_pdl(splitk_reduce_ln_kernel<8>, g, dim3(256), 0, st, sh, ep);
+          default: return cudaErrorInvalidValue;
+        }
+      }
+    }
     const int ncols = EPI == EPI_GEGLU ? ep.geglu_I : sh.N;
     const long long threads = (long long)sh.M * (ncols / 64) * 8;
     return launch_pdl(splitk_reduce_kernel<EPI>, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, st, sh, ep);
@@ -790,6 +840,11 @@ cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
                         (ep.out_mode == OUT_BF16X2 && ep.kind != EPI_RESID && sh.dst_plane % 4 != 0)))
     return cudaErrorInvalidValue;
   if (sh.N % 64 != 0 || sh.K % 8 != 0 || (sh.nseg != 1 && sh.nseg != 3)) return cudaErrorInvalidValue;
+  if (ep.ln_w && (ep.kind != EPI_RESID || sh.splits < 2 || sh.N % 256 != 0 || sh.N > 1024 || !ep.ln_out ||
+                  (ep.ln_planes != 1 && ep.ln_planes != 2) ||
+                  ((reinterpret_cast<uintptr_t>(ep.ln_w) | reinterpret_cast<uintptr_t>(ep.ln_out)) & 15) != 0 ||
+                  (ep.ln_planes == 2 && ep.ln_plane % 8 != 0)))
+    return cudaErrorInvalidValue;
   if (ep.kind == EPI_GEGLU && (ep.geglu_I % 64 != 0 || sh.N != 2 * ep.geglu_I)) return cudaErrorInvalidValue;
   if (ep.kind == EPI_ROPE && (ep.rope_cols % 64 != 0 || !ep.pos || !ep.cos_t || !ep.sin_t))
     return cudaErrorInvalidValue;

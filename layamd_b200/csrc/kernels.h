@@ -70,6 +70,14 @@ struct GemmEpi {
   const int* pos = nullptr;      // EPI_ROPE: position of each row within its sequence
   int rope_cols = 0;             // EPI_ROPE: rotate columns [0, rope_cols) (q and k), head dim 64
   int geglu_I = 0;               // EPI_GEGLU: output width I (a multiple of 64)
+  // EPI_RESID with split-K only (GemmShape::splits > 1): the reduce kernel also writes
+  // ln_out = LayerNorm(x) * ln_w (no bias) as bf16 planes (ln_planes of them, ln_plane elements
+  // apart) from the new x of each row, the LayerNorm kernel's arithmetic; N a multiple of 128, <= 1024.
+  const float* ln_w = nullptr;
+  float ln_eps = 1e-5f;
+  bf16* ln_out = nullptr;
+  long long ln_plane = 0;
+  int ln_planes = 1;
 };
 
 // Output map of the GEMM epilogue over [planes][rows][ld] (bf16) or [rows][ld] (fp32, planes 1):

@@ -18,38 +18,6 @@
 namespace laya {
 namespace {
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
-template <int NV>
-__device__ __forceinline__ void layer_norm_regs(float4 (&v)[NV], const float* w, const float* b, float eps, int D,
-                                                int lane) {
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-  const float mean = warp_sum(s) / D;
-  float q = 0.f;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    v[i].x -= mean; v[i].y -= mean; v[i].z -= mean; v[i].w -= mean;
-    q += (v[i].x * v[i].x + v[i].y * v[i].y) + (v[i].z * v[i].z + v[i].w * v[i].w);
-  }
-  const float rstd = 1.f / sqrtf(warp_sum(q) / D + eps);
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const float4 g = reinterpret_cast<const float4*>(w)[lane + 32 * i];
-    float4 r = make_float4(v[i].x * rstd * g.x, v[i].y * rstd * g.y, v[i].z * rstd * g.z, v[i].w * rstd * g.w);
-    if (b) {
-      const float4 bb = reinterpret_cast<const float4*>(b)[lane + 32 * i];
-      r.x += bb.x; r.y += bb.y; r.z += bb.z; r.w += bb.w;
-    }
-    v[i] = r;
-  }
-}
-
 template <int NV>
 __global__ void __launch_bounds__(256) ln_kernel(const LnArgs a) {
   pdl_trigger();
@@ -89,18 +57,8 @@ __global__ void __launch_bounds__(256) ln_kernel(const LnArgs a) {
   }
   if (a.out_bf) {
     if (a.w2) layer_norm_regs<NV>(v, a.w2, a.b2, a.eps2, D, lane);
-    uint2* hi = reinterpret_cast<uint2*>(a.out_bf + (long long)row * D);
-    uint2* lo = reinterpret_cast<uint2*>(a.out_bf + a.out_plane + (long long)row * D);
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const uint32_t h0 = pack_bf16x2(v[i].x, v[i].y), h1 = pack_bf16x2(v[i].z, v[i].w);
-      hi[lane + 32 * i] = make_uint2(h0, h1);
-      if (a.out_planes == 2) {
-        const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h0));
-        const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h1));
-        lo[lane + 32 * i] = make_uint2(pack_bf16x2(v[i].x - f0.x, v[i].y - f0.y), pack_bf16x2(v[i].z - f1.x, v[i].w - f1.y));
-      }
-    }
+    store_bf16_planes<NV>(v, a.out_bf + (long long)row * D, a.out_bf + a.out_plane + (long long)row * D, a.out_planes,
+                          lane);
   }
 }
 

@@ -347,3 +347,19 @@ def test_stage_replay_matches_forward(large_bf16):
     ac2 = np.zeros_like(ac)
     assert L.laya_staged_results(large_bf16.h, lo2.ctypes.data_as(FP), ac2.ctypes.data_as(FP)) == 0
     assert rel(lo2, lo) < 1e-5 and rel(ac2, ac) < 1e-5
+
+
+def test_split_k_layernorm_fusion_is_exact(large_ckpt, large_bf16):
+    """At 512 rows the MLP-out GEMM runs split-K, and its reduce kernel also writes the next layer's
+    attention LayerNorm. With that fusion off (LAYA_SPLIT_LN=0) the LayerNorm kernel computes the same
+    rows from the same x with the same arithmetic: the same bits out."""
+    qs = workloads.c1(synth.ARCHS["large"])
+    rc, lo, ac = large_bf16.forward(qs)
+    assert rc == 0
+    h = Handle(large_ckpt, 0, env={"LAYA_MAX_TOKENS": 65536, "LAYA_SPLIT_LN": 0})
+    try:
+        rc2, lo2, ac2 = h.forward(qs)
+    finally:
+        h.close()
+    assert rc2 == 0
+    assert np.array_equal(lo, lo2) and np.array_equal(ac, ac2)
