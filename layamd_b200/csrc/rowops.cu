@@ -30,7 +30,7 @@ __global__ void __launch_bounds__(256) ln_kernel(const LnArgs a) {
   const float4* src = reinterpret_cast<const float4*>(a.src + src_row * D);
   float4 v[NV];
 #pragma unroll
-  for (int i = 0; i < NV; ++i) v[i] = src[lane + 32 * i];
+  for (int i = 0; i < NV; ++i) v[i] = __ldcs(src + lane + 32 * i);  // read once: evict-first
   if (a.copy_f32) {
     float4* c = reinterpret_cast<float4*>(a.copy_f32 + (long long)row * D);
 #pragma unroll
