@@ -123,7 +123,14 @@ class Replica {
   float* ws = nullptr;
   size_t ws_floats = 0;
   bool use_splitk = true;
-  bool split_ln = true;  // LAYA_SPLIT_LN=0: a split-K residual GEMM leaves its LayerNorm to the LN kernel
+  // LAYA_SPLIT_LN=0: a split-K residual GEMM leaves its LayerNorm to the LN kernel (same K split)
+  bool split_ln = true;
+  // K-block times credited to a split whose reduce kernel can absorb the following LayerNorm launch:
+  // the split costs the partials' round trip and the reduce kernel (28) but saves the LayerNorm
+  // launch, leaving about 8. Measured at 512 rows (ModernBERT-large, one B200): the attention
+  // out-projection then splits 4 ways with the MLP LayerNorm in its reduce, 1.774 -> 1.687 ms per
+  // pass. LAYA_SPLIT_LN_CREDIT overrides.
+  int split_ln_credit = 20;
   cudaStream_t st = nullptr;
   std::vector<void*> allocs;
   std::vector<void*> host_allocs;
@@ -394,6 +401,7 @@ class Replica {
     // whose partials a second kernel sums in order. 32 M floats (128 MB) cover every split count.
     use_splitk = !(getenv("LAYA_SPLITK") && atoi(getenv("LAYA_SPLITK")) == 0);
     split_ln = !(getenv("LAYA_SPLIT_LN") && atoi(getenv("LAYA_SPLIT_LN")) == 0);
+    if (getenv("LAYA_SPLIT_LN_CREDIT")) split_ln_credit = atoi(getenv("LAYA_SPLIT_LN_CREDIT"));
     if (use_splitk) {
       ws_floats = (size_t)32 << 20;
       if (!dalloc(&ws, ws_floats * 4, err)) return false;
@@ -540,15 +548,16 @@ class Replica {
     bool ln_fused = false;
     if (bn == 128 && use_splitk) {
       // too few 128 x 128 tiles to fill the GPU: split the K loop (deterministic partial sums)
+      const bool ln_fusable = ln_w && ep.kind == EPI_RESID && W.N % 256 == 0 && W.N <= 1024;
       const int tiles = ((M + 127) / 128) * ((W.N + 127) / 128);
-      int s = splitk_choose(tiles, ((W.K + 63) / 64) * nseg, num_sms);
+      int s = splitk_choose(tiles, ((W.K + 63) / 64) * nseg, num_sms, ln_fusable ? split_ln_credit : 0);
       while (s > 1 && splitk_ws_floats(M, W.N, s) > ws_floats) --s;
       if (s > 1) {
         sh.splits = s;
         sh.ws = ws;
         sh.dst = dst;
         sh.dst_plane = dst_plane;
-        if (ln_w && split_ln && ep.kind == EPI_RESID && W.N % 256 == 0 && W.N <= 1024) {
+        if (ln_fusable && split_ln) {
           ep.ln_w = ln_w;
           ep.ln_eps = cfg.norm_eps;
           ep.ln_out = xn.p;
@@ -684,8 +693,9 @@ class Replica {
       stage(glob ? "attn_global" : "attn_sliding", [&] {
         attend_rows(items, L.items_cap, items128, L.items128_cap, soff, slen, glob ? 0 : cfg.local_attention / 2);
       });
-      stage("gemm_attn_out", [&] { gemm(ao, M, enc[l].Wo, out_x, x, 0, epi_resid(nullptr)); });
-      stage("ln", [&] {
+      bool mlp_ln_done = false;  // the MLP LayerNorm, fused into a split-K reduce
+      stage("gemm_attn_out", [&] { mlp_ln_done = gemm(ao, M, enc[l].Wo, out_x, x, 0, epi_resid(nullptr), enc[l].mlp_norm); });
+      if (!mlp_ln_done) stage("ln", [&] {
         LnArgs a = ln_base(M);
         a.src = x;
         a.w = enc[l].mlp_norm;

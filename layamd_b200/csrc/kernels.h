@@ -42,16 +42,18 @@ inline size_t splitk_ws_floats(int M, int N, int splits) { return (size_t)splits
 // loop in K-block times plus the partials' round trip through memory and the reduce kernel, which
 // measured about 28 K-block times (11 us) on B200 at 512 rows. At least 4 K blocks per slice; 1 when
 // the tiles already fill the GPU. At 512 rows this splits the long-K GEMMs (MLP-out, K = 2624; the
-// head's FFN-2, K = 4096) and keeps whole-K tiles for K = 1024.
+// head's FFN-2, K = 4096) and keeps whole-K tiles for K = 1024. `credit`: K-block times that a split
+// saves elsewhere — a LayerNorm launch that the reduce kernel absorbs (a residual GEMM followed by a
+// LayerNorm), subtracted from every S > 1.
 constexpr int kSplitReduceBlocks = 28;
-inline int splitk_choose(int tiles, int kblocks, int sms) {
+inline int splitk_choose(int tiles, int kblocks, int sms, int credit = 0) {
   if (tiles >= sms) return 1;
   int best = 1;
   long long best_cost = kblocks;
   for (int s = 2; s <= kMaxSplits; ++s) {
     if (kblocks / s < 4) break;
     const long long waves = (tiles * s + sms - 1) / sms;
-    const long long cost = waves * ((kblocks + s - 1) / s) + kSplitReduceBlocks;
+    const long long cost = waves * ((kblocks + s - 1) / s) + kSplitReduceBlocks - credit;
     if (cost < best_cost) { best_cost = cost; best = s; }
   }
   return best;

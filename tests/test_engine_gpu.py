@@ -350,9 +350,10 @@ def test_stage_replay_matches_forward(large_bf16):
 
 
 def test_split_k_layernorm_fusion_is_exact(large_ckpt, large_bf16):
-    """At 512 rows the MLP-out GEMM runs split-K, and its reduce kernel also writes the next layer's
-    attention LayerNorm. With that fusion off (LAYA_SPLIT_LN=0) the LayerNorm kernel computes the same
-    rows from the same x with the same arithmetic: the same bits out."""
+    """At 512 rows the attention-out and MLP-out GEMMs run split-K, and their reduce kernels also write
+    the LayerNorm that follows (the MLP norm, the next layer's attention norm). With that fusion off
+    (LAYA_SPLIT_LN=0: the same K splits) the LayerNorm kernel computes the same rows from the same x
+    with the same arithmetic: the same bits out."""
     qs = workloads.c1(synth.ARCHS["large"])
     rc, lo, ac = large_bf16.forward(qs)
     assert rc == 0
