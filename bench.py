@@ -11,6 +11,9 @@ Per step (one forward pass over the 192 questions):
          CUDA graph, timed with CUDA events on the engine's stream (laya_replay), max over ranks;
   e2e    decisions/s through the public C ABI (laya_forward_batch) from host arrays: packing,
          host->device upload, the pass and the device->host read of the logits every step.
+  roofline  the encoder GEMM family: algorithmic 2*M*N*K FLOPs of one pass over their device time,
+         from CUDA events around every stage inside the replayed pass graph (laya_replay_profiled),
+         against the measured sustained bf16 peak of MEASURED_PEAKS.json.
 Multi-GPU (torchrun, one rank per GPU): every rank serves its own 192 questions on its own GPU;
 questions are independent, so there is no collective on the data path (weak scaling). Ranks only
 meet at barriers and for the max-over-ranks timing reduction (gloo).
@@ -172,27 +175,22 @@ def load_peaks():
         return 1400.0, "fallback (1.4 PFLOP/s sustained)"
 
 
-def profiled_gemm_time(L, h, lens, ids, nmark, markers, qtypes, n_act, calls=2):
-    """Average device time of the encoder GEMM launches, CUDA events around each launch on the engine's
-    stream (eager launches with profiling on), summed per GEMM class."""
-    IP = ctypes.POINTER(ctypes.c_int)
-    FP = ctypes.POINTER(ctypes.c_float)
-    lo = np.zeros(int(nmark.sum()), np.float32)
-    ac = np.zeros((len(lens), n_act), np.float32)
-    L.laya_prof_enable(h, 1)
+STAGES = ["gemm_qkv", "gemm_attn_out", "gemm_mlp_in", "gemm_mlp_out", "attn_global", "attn_sliding", "ln",
+          "embed_ln", "head_gemm", "head_attn", "head_ln", "scorer", "head_out"]
+
+
+def profiled_stage_times(L, h, iters=5):
+    """Device time per stage of one pass (ms) and its launches: the staged pass replayed `iters` times
+    back to back as a graph with a CUDA event pair around every stage (laya_replay_profiled), read
+    from the last replay, so the kernels run in the same steady state as the timed replays."""
     L.laya_prof_reset(h)
-    for _ in range(calls):
-        L.laya_forward_batch(h, len(lens), lens.ctypes.data_as(IP), ids.ctypes.data_as(IP), nmark.ctypes.data_as(IP),
-                             markers.ctypes.data_as(IP), qtypes.ctypes.data_as(IP), lo.ctypes.data_as(FP),
-                             ac.ctypes.data_as(FP))
+    assert L.laya_replay_profiled(h, iters) == 0, "laya_replay_profiled failed"
     out = {}
-    for name in ["gemm_qkv", "gemm_attn_out", "gemm_mlp_in", "gemm_mlp_out", "attn_global", "attn_sliding", "ln",
-                 "embed_ln", "head_gemm", "head_attn", "head_ln", "scorer", "head_out"]:
+    for name in STAGES:
         ms = ctypes.c_double(0)
         n = ctypes.c_longlong(0)
         if L.laya_prof_get(h, name.encode(), ctypes.byref(ms), ctypes.byref(n)) == 0:
-            out[name] = (ms.value / calls, n.value // calls)
-    L.laya_prof_enable(h, 0)
+            out[name] = (ms.value, n.value)
     L.laya_prof_reset(h)
     return out
 
@@ -302,6 +300,7 @@ def main():
     assert rc == 0, "laya_stage failed: %d" % rc
     ms = ctypes.c_double(0)
     assert L.laya_replay(h, args.warmup, ctypes.byref(ms)) == 0
+    assert L.laya_replay_profiled(h, 1) == 0  # captures the profiled copy of the pass graph up front
     L.laya_io_stats(h, None, None, None, 1)
     dist.barrier()
     with ClockSampler(local) as clk:
@@ -329,8 +328,9 @@ def main():
     L.laya_io_stats(h, None, ctypes.byref(h2d), ctypes.byref(d2h), 1)
     clocks = clk.summary()
 
-    # ---- roofline of the dominant kernel (the tcgen05 GEMM), profiled pass after the timed region
-    prof = profiled_gemm_time(L, h, lens, ids, nmark, markers, qtypes, n_act)
+    # ---- roofline of the dominant kernel (the tcgen05 GEMM): per-stage CUDA events inside the
+    # replayed pass graph, right after the timed region and the end-to-end calls (steady clocks)
+    prof = profiled_stage_times(L, h)
     fl = encoder_gemm_flops(qs, arch)
     g_ms = sum(prof[k][0] for k in fl if k in prof)
     g_launch = sum(prof[k][1] for k in fl if k in prof)
@@ -389,6 +389,8 @@ def main():
             "model_flops_per_step": decision_flops(qs, arch),
             "model_tflops": decision_flops(qs, arch) * world / (dev_ms / args.steps / 1e3) / 1e12,
             "stages_ms": {k: round(v[0], 4) for k, v in prof.items()},
+            "stages_note": "device time per pass of each stage, CUDA events around every stage inside the replayed "
+                           "pass graph (laya_replay_profiled), last of 5 back-to-back replays after the timed region",
             "clocks": clocks, "latency": lat, "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)

@@ -97,6 +97,11 @@ int laya_stage(void* h, int B, const int* lens, const int* ids, const int* nmark
                const int* qtypes);
 int laya_replay(void* h, int iters, double* ms);
 int laya_staged_results(void* h, float* logits, float* act);
+/* Benchmark support (no counterpart in the reference): replays the staged pass `iters` times back
+ * to back as a second graph that also records a CUDA event pair around every stage, and adds the
+ * stage times of the last replay to the profile table read by laya_prof_get, so that per-stage device
+ * times are taken in the same steady state as laya_replay. Return 0 or a negative error. */
+int laya_replay_profiled(void* h, int iters);
 
 /* Cumulative counters of the forward and replay calls since the last reset, summed over devices:
  * kernel launches of this library, bytes copied host->device and device->host. reset != 0 clears

@@ -124,6 +124,11 @@ int laya_replay(void* h, int iters, double* ms) {
   return E(h)->replay(iters, ms);
 }
 
+int laya_replay_profiled(void* h, int iters) {
+  if (!h || iters < 0) return -1;
+  return E(h)->replay_profiled(iters);
+}
+
 int laya_staged_results(void* h, float* logits, float* act) {
   if (!h || !logits || !act) return -1;
   return E(h)->staged_results(logits, act);

@@ -189,6 +189,10 @@ class Replica {
   std::vector<Question> staged;
   PassPlan staged_plan;
   cudaGraphExec_t staged_graph = nullptr;
+  // the same pass captured with an event pair around every stage (laya_replay_profiled)
+  cudaGraphExec_t staged_prof_graph = nullptr;
+  std::vector<std::tuple<const char*, cudaEvent_t, cudaEvent_t>> staged_prof_events;
+  bool capturing_prof = false;
 
   Replica(Engine& e, int d) : E(e), cfg(e.cfg), dev(d) {}
   ~Replica() { release(); }
@@ -200,6 +204,7 @@ class Replica {
     graphs.clear();
     if (staged_graph) cudaGraphExecDestroy(staged_graph);
     staged_graph = nullptr;
+    drop_staged_profile();
     for (auto ev : ev_pool) cudaEventDestroy(ev);
     ev_pool.clear();
     for (void* p : allocs) cudaFree(p);
@@ -497,17 +502,36 @@ class Replica {
   template <typename F>
   void stage(const char* name, F&& fn) {
     const bool timed = E.prof_on && !capturing;
+    const bool graph_timed = capturing && capturing_prof;  // event-record nodes in the captured graph
     cudaEvent_t a = nullptr, b = nullptr;
     if (timed) {
       a = take_event();
       b = take_event();
       cudaEventRecord(a, st);
+    } else if (graph_timed) {
+      cudaEventCreate(&a);
+      cudaEventCreate(&b);
+      // external records become event-record nodes of the graph (a plain record inside a capture
+      // only orders work within the capture)
+      chk(cudaEventRecordWithFlags(a, st, cudaEventRecordExternal));
     }
     fn();
     if (timed) {
       cudaEventRecord(b, st);
       prof_pending.emplace_back(name, a, b);
+    } else if (graph_timed) {
+      chk(cudaEventRecordWithFlags(b, st, cudaEventRecordExternal));
+      staged_prof_events.emplace_back(name, a, b);
     }
+  }
+  void drop_staged_profile() {
+    if (staged_prof_graph) cudaGraphExecDestroy(staged_prof_graph);
+    staged_prof_graph = nullptr;
+    for (auto& t : staged_prof_events) {
+      cudaEventDestroy(std::get<1>(t));
+      cudaEventDestroy(std::get<2>(t));
+    }
+    staged_prof_events.clear();
   }
   void prof_collect() {
     for (auto& t : prof_pending) {
@@ -925,6 +949,7 @@ class Replica {
     if (cudaSetDevice(dev) != cudaSuccess) return -2;
     staged = qs;
     if (staged_graph) { cudaGraphExecDestroy(staged_graph); staged_graph = nullptr; }
+    drop_staged_profile();
     if (qs.empty()) return 0;
     std::vector<int> lens(qs.size()), nms(qs.size());
     for (size_t i = 0; i < qs.size(); ++i) { lens[i] = qs[i].len; nms[i] = qs[i].nmark; }
@@ -976,6 +1001,55 @@ class Replica {
     int herr = 0;
     cudaMemcpy(&herr, d_err, 4, cudaMemcpyDeviceToHost);
     return first_err == cudaSuccess && herr == 0 ? 0 : -2;
+  }
+  // Replays the staged pass `iters` times back to back as a graph that also records an event pair
+  // around every stage, then adds the last replay's stage times to the profile table (prof_acc).
+  int replay_profiled(int iters) {
+    if (staged.empty() || iters < 1) return 0;
+    if (!staged_graph) return -4;
+    if (cudaSetDevice(dev) != cudaSuccess) return -2;
+    first_err = cudaSuccess;
+    if (!staged_prof_graph) {
+      cudaGraph_t g = nullptr;
+      if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return -2;
+      capturing = true;
+      capturing_prof = true;
+      enqueue(staged_plan, false, false);
+      capturing = false;
+      capturing_prof = false;
+      if (cudaStreamEndCapture(st, &g) != cudaSuccess || first_err != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        drop_staged_profile();
+        return -2;
+      }
+      const cudaError_t ie = cudaGraphInstantiate(&staged_prof_graph, g, 0);
+      cudaGraphDestroy(g);
+      if (ie != cudaSuccess) {
+        staged_prof_graph = nullptr;
+        drop_staged_profile();
+        return -2;
+      }
+    }
+    fill(staged_plan, staged.data());
+    if (cudaMemcpy(d_meta, h_meta, meta_layout(staged_plan.Tpad, staged_plan.n, staged_plan.R).total * 4,
+                   cudaMemcpyHostToDevice) != cudaSuccess)
+      return -2;
+    for (int i = 0; i < iters; ++i) chk(cudaGraphLaunch(staged_prof_graph, st));
+    n_launches += (long long)iters * staged_launches;
+    chk(cudaStreamSynchronize(st));
+    if (first_err != cudaSuccess) return -2;
+    for (auto& t : staged_prof_events) {
+      float ms = 0.f;
+      if (cudaEventElapsedTime(&ms, std::get<1>(t), std::get<2>(t)) != cudaSuccess) return -2;
+      const std::string n = std::get<0>(t);
+      bool found = false;
+      for (auto& kv : prof_acc)
+        if (kv.first == n) { kv.second.first += ms; kv.second.second += 1; found = true; break; }
+      if (!found) prof_acc.push_back({n, {(double)ms, 1}});
+    }
+    int herr = 0;
+    cudaMemcpy(&herr, d_err, 4, cudaMemcpyDeviceToHost);
+    return herr == 0 ? 0 : -2;
   }
   int staged_results() {
     if (staged.empty()) return 0;
@@ -1141,6 +1215,16 @@ int Engine::replay(int iters, double* ms) {
   for (size_t i = 0; i < reps.size(); ++i) th.emplace_back([&, i] { rc[i] = reps[i]->replay(iters, &t[i]); });
   for (auto& x : th) x.join();
   *ms = *std::max_element(t.begin(), t.end());
+  for (int r : rc)
+    if (r) return r;
+  return 0;
+}
+
+int Engine::replay_profiled(int iters) {
+  std::vector<int> rc(reps.size(), 0);
+  std::vector<std::thread> th;
+  for (size_t i = 0; i < reps.size(); ++i) th.emplace_back([&, i] { rc[i] = reps[i]->replay_profiled(iters); });
+  for (auto& x : th) x.join();
   for (int r : rc)
     if (r) return r;
   return 0;

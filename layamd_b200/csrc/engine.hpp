@@ -89,6 +89,7 @@ class Engine {
                     float* logits, float* act);
   int stage(int B, const int* lens, const int* ids, const int* nmark, const int* markers, const int* qtypes);
   int replay(int iters, double* ms);
+  int replay_profiled(int iters);
   int staged_results(float* logits, float* act);
   void prof_report(int iters);
   void prof_reset();

@@ -347,6 +347,22 @@ def test_stage_replay_matches_forward(large_bf16):
     ac2 = np.zeros_like(ac)
     assert L.laya_staged_results(large_bf16.h, lo2.ctypes.data_as(FP), ac2.ctypes.data_as(FP)) == 0
     assert rel(lo2, lo) < 1e-5 and rel(ac2, ac) < 1e-5
+    # the profiled copy of the staged graph: the same results, and one timed entry per stage per pass
+    # (the last replay's)
+    L.laya_prof_reset(large_bf16.h)
+    assert L.laya_replay_profiled(large_bf16.h, 2) == 0
+    lo3 = np.zeros_like(lo)
+    ac3 = np.zeros_like(ac)
+    assert L.laya_staged_results(large_bf16.h, lo3.ctypes.data_as(FP), ac3.ctypes.data_as(FP)) == 0
+    assert np.array_equal(lo3, lo2) and np.array_equal(ac3, ac2)
+    for name in (b"gemm_qkv", b"gemm_mlp_in", b"attn_global", b"attn_sliding"):
+        t, n = ctypes.c_double(0), ctypes.c_longlong(0)
+        assert L.laya_prof_get(large_bf16.h, name, ctypes.byref(t), ctypes.byref(n)) == 0
+        assert t.value > 0
+    t, n = ctypes.c_double(0), ctypes.c_longlong(0)
+    L.laya_prof_get(large_bf16.h, b"gemm_qkv", ctypes.byref(t), ctypes.byref(n))
+    assert n.value == synth.ARCHS["large"].layers
+    L.laya_prof_reset(large_bf16.h)
 
 
 def test_split_k_layernorm_fusion_is_exact(large_ckpt, large_bf16):
