@@ -146,6 +146,14 @@ int laya_b200_gemm_splitk(const void* A, const void* W, void* out, float* resid,
 int laya_b200_attention(const void* qkv, void* out, int rows, int B, const int* lens, int H, int window, int impl,
                         void* stream, int sync);
 
+/* No counterpart in the reference (whose engine exits on any GPU error). Exercises, on GPU `device`,
+ * the bounded wait that every pipeline kernel of this library uses on its mbarriers: one thread waits
+ * on a barrier phase that nothing completes, gives up after the wait budget (about 2^31 SM cycles,
+ * roughly one second), records its error code in a device word and returns, so the kernel ends
+ * normally and the context stays usable. Writes the recorded code (30) to *code, the wait's length in
+ * SM cycles to *cycles and the kernel's device time to *ms. Returns 0, or -2 if a CUDA call failed. */
+int laya_b200_watchdog_selftest(int device, int* code, long long* cycles, float* ms);
+
 /* No counterpart in the reference. laya_b200_gemm_splitk for callers that cannot allocate device
  * memory: a host whose memory manager reserves the GPU's memory up front (a serving stack with a
  * caching allocator) or a plugin host that forbids allocation in its callbacks, where a cudaMalloc

@@ -22,6 +22,7 @@ enum DevErr : int {
   kErrAttnLoad = 16,     // attention producer timed out waiting for a K / V buffer to be released
   kErrAttnMma = 17,      // attention MMA issuer timed out waiting for Q / K / V / P
   kErrAttnSoftmax = 18,  // attention softmax warps timed out waiting for S or O
+  kErrSelfTest = 30,     // watchdog self-test: a wait on a barrier phase that nothing completes
 };
 
 // ---------------------------------------------------------------- programmatic dependent launch
