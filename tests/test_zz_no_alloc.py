@@ -6,7 +6,8 @@ scratch is a fixed array in the library's device image instead of a cudaMalloc'd
 checks call it through the C ABI twice in a row, on two different problems, and compare each result
 with the allocating entry point laya_b200_gemm_splitk and with an fp64 reference, at the tolerances
 of the other GEMM tests (1e-4 relative for fp32 results, 1e-2 for bf16). The second call inherits the
-array from the first, so it also checks that stale counters do not leak into a later call. This file
+array from the first (partials and error word), so it also checks that nothing a call leaves there
+leaks into the next one. This file
 sorts last so that a run stopping at its first failure has already run every other test.
 """
 import ctypes
