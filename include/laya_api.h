@@ -84,6 +84,16 @@ int laya_plan_passes(void* h, int B, const int* lens, const int* nmark, const in
 int laya_plan_passes_cfg(int max_len, int pass_tokens, int max_seqs, int B, const int* lens, const int* nmark,
                          const int* markers, int cap, int* pass_first, int* pass_count, int* pass_rows);
 
+/* The engine's plan for one GEMM launch, host-only (no counterpart in the reference, which autotunes
+ * per shape at start-up, src/engine.hip:293-379): *bn = 128 or 256 (one CTA per 128 x bn tile) or
+ * 512 (a CTA pair per 256 x 256 tile), *splits = K slices (1 = whole K). M packed rows, the weight's
+ * N x K, parity != 0 for the fp32-parity mode (three bf16 products per K block), the device's SM count
+ * and co-resident CTA pairs, ln_fusable != 0 for a residual GEMM whose following bias-free LayerNorm
+ * a split's reduce kernel can take over (with the default credit; LAYA_SPLIT_LN_CREDIT changes only
+ * the engine's own choice). Returns 0 or -1. */
+int laya_plan_gemm(int M, int N, int K, int parity, int num_sms, int pair_clusters, int ln_fusable, int* bn,
+                   int* splits);
+
 /* The replica (0..ndev-1) each of B questions goes to when a call is sharded over ndev GPUs, as
  * laya_forward_batch does it; host-only. Returns 0 or -1. */
 int laya_shard_plan(int ndev, int B, const int* lens, int* owner);

@@ -56,6 +56,7 @@ def load_lib(path: str = LIB_PATH) -> ctypes.CDLL:
         "laya_stage": (i, [vp, i, _IP, _IP, _IP, _IP, _IP]),
         "laya_replay": (i, [vp, i, ctypes.POINTER(d)]),
         "laya_replay_profiled": (i, [vp, i]),
+        "laya_plan_gemm": (i, [i, i, i, i, i, i, i, _IP, _IP]),
         "laya_b200_watchdog_selftest": (i, [i, ctypes.POINTER(i), ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(f)]),
         "laya_staged_results": (i, [vp, _FP, _FP]),
         "laya_set_dump_dir": (i, [vp, ctypes.c_char_p]),

@@ -6,6 +6,7 @@
 #include <vector>
 
 #include "engine.hpp"
+#include "kernels.h"
 #include "laya_api.h"
 
 using laya::Engine;
@@ -110,6 +111,16 @@ int laya_plan_passes(void* h, int B, const int* lens, const int* nmark, const in
 int laya_shard_plan(int ndev, int B, const int* lens, int* owner) {
   if (ndev < 1 || B < 0 || (B > 0 && (!lens || !owner))) return -1;
   laya::shard_owners(B, lens, ndev, owner);
+  return 0;
+}
+
+int laya_plan_gemm(int M, int N, int K, int parity, int num_sms, int pair_clusters, int ln_fusable, int* bn,
+                   int* splits) {
+  if (M <= 0 || N <= 0 || K <= 0 || num_sms <= 0 || pair_clusters < 0 || !bn || !splits) return -1;
+  const laya::GemmPlan p = laya::gemm_plan(M, N, K, parity ? 3 : 1, num_sms, pair_clusters, true, laya::kSplitWsFloats,
+                                           ln_fusable ? laya::kSplitLnCredit : 0);
+  *bn = p.bn;
+  *splits = p.splits;
   return 0;
 }
 

@@ -125,12 +125,9 @@ class Replica {
   bool use_splitk = true;
   // LAYA_SPLIT_LN=0: a split-K residual GEMM leaves its LayerNorm to the LN kernel (same K split)
   bool split_ln = true;
-  // K-block times credited to a split whose reduce kernel can absorb the following LayerNorm launch:
-  // the split costs the partials' round trip and the reduce kernel (28) but saves the LayerNorm
-  // launch, leaving about 8. Measured at 512 rows (ModernBERT-large, one B200): the attention
-  // out-projection then splits 4 ways with the MLP LayerNorm in its reduce, 1.774 -> 1.687 ms per
-  // pass. LAYA_SPLIT_LN_CREDIT overrides.
-  int split_ln_credit = 20;
+  // K-block times credited to a split whose reduce kernel can absorb the following LayerNorm launch
+  // (kSplitLnCredit; LAYA_SPLIT_LN_CREDIT overrides)
+  int split_ln_credit = kSplitLnCredit;
   cudaStream_t st = nullptr;
   std::vector<void*> allocs;
   std::vector<void*> host_allocs;
@@ -408,7 +405,7 @@ class Replica {
     split_ln = !(getenv("LAYA_SPLIT_LN") && atoi(getenv("LAYA_SPLIT_LN")) == 0);
     if (getenv("LAYA_SPLIT_LN_CREDIT")) split_ln_credit = atoi(getenv("LAYA_SPLIT_LN_CREDIT"));
     if (use_splitk) {
-      ws_floats = (size_t)32 << 20;
+      ws_floats = kSplitWsFloats;
       if (!dalloc(&ws, ws_floats * 4, err)) return false;
     }
     const MetaLayout L = meta_layout(Tcap, Bcap, Rcap);
@@ -547,48 +544,33 @@ class Replica {
     ev_used = 0;
   }
 
-  // Tile per launch: the CTA-pair 256 x 256 tile when its tile count fills every co-resident pair
-  // twice, else 128 x 256, else 128 x 128 (more tiles for small M).
-  int pick_tile(int M, const Mat& W) const {
-    if (W.N < 256) return 128;
-    const long long tp = (long long)((M + 255) / 256) * ((W.N + 255) / 256);
-    if (pair_clusters > 0 && tp >= 2LL * pair_clusters) return kGemmPair;
-    // whole waves of 128 x 128 against 128 x 256 tiles; a 128 x 256 tile costs about 1.6 of the
-    // narrow one (it reads each A block once per 256 columns): at 512 rows the GeGLU GEMM runs one
-    // wave of 84 wide tiles in 13 us against two waves of 164 narrow ones in 17 us
-    const long long rows = (M + 127) / 128;
-    const long long w128 = (rows * ((W.N + 127) / 128) + num_sms - 1) / num_sms;
-    const long long w256 = (rows * ((W.N + 255) / 256) + num_sms - 1) / num_sms;
-    return 10 * w128 > 16 * w256 ? 256 : 128;
-  }
   // out: the epilogue's output map; dst / dst_plane: the buffer it covers (for a split-K launch,
   // whose epilogue runs in a second kernel on plain pointers). ln_w: for a residual GEMM, the gain of
   // the LayerNorm that follows it into xn; when the GEMM runs split-K, its reduce kernel writes that
   // LayerNorm too and gemm() returns true (the caller then skips its LayerNorm launch).
   bool gemm(const Operand& A, int M, const Mat& W, const CUtensorMap& out, void* dst, long long dst_plane,
             GemmEpi ep, const float* ln_w = nullptr) {
-    int bn = pick_tile(M, W);
+    // a residual GEMM followed by a bias-free LayerNorm over at most 1024 columns: a split-K reduce
+    // kernel can write that LayerNorm too
+    const bool ln_fusable = ln_w && ep.kind == EPI_RESID && W.N % 256 == 0 && W.N <= 1024;
+    const GemmPlan plan = gemm_plan(M, W.N, W.K, nseg, num_sms, pair_clusters, use_splitk, ws_floats,
+                                    ln_fusable ? split_ln_credit : 0);
+    const int bn = plan.bn;
     GemmShape sh{M, W.N, W.K, nseg};
     bool ln_fused = false;
-    if (bn == 128 && use_splitk) {
-      // too few 128 x 128 tiles to fill the GPU: split the K loop (deterministic partial sums)
-      const bool ln_fusable = ln_w && ep.kind == EPI_RESID && W.N % 256 == 0 && W.N <= 1024;
-      const int tiles = ((M + 127) / 128) * ((W.N + 127) / 128);
-      int s = splitk_choose(tiles, ((W.K + 63) / 64) * nseg, num_sms, ln_fusable ? split_ln_credit : 0);
-      while (s > 1 && splitk_ws_floats(M, W.N, s) > ws_floats) --s;
-      if (s > 1) {
-        sh.splits = s;
-        sh.ws = ws;
-        sh.dst = dst;
-        sh.dst_plane = dst_plane;
-        if (ln_fusable && split_ln) {
-          ep.ln_w = ln_w;
-          ep.ln_eps = cfg.norm_eps;
-          ep.ln_out = xn.p;
-          ep.ln_plane = xn.plane;
-          ep.ln_planes = P;
-          ln_fused = true;
-        }
+    if (plan.splits > 1) {
+      // too few 128 x 128 tiles to fill the GPU: the K loop in slices (deterministic partial sums)
+      sh.splits = plan.splits;
+      sh.ws = ws;
+      sh.dst = dst;
+      sh.dst_plane = dst_plane;
+      if (ln_fusable && split_ln) {
+        ep.ln_w = ln_w;
+        ep.ln_eps = cfg.norm_eps;
+        ep.ln_out = xn.p;
+        ep.ln_plane = xn.plane;
+        ep.ln_planes = P;
+        ln_fused = true;
       }
     }
     launched(gemm_launch(A.map, bn == 256 ? W.m256 : W.m128, out, bn, sh, ep, d_err, num_sms, st));

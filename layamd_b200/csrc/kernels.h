@@ -35,6 +35,9 @@ struct GemmShape {
   long long dst_plane = 0;
 };
 constexpr int kMaxSplits = 8;
+// Split-K workspace of an engine replica (fp32 partials): 32 Mi floats (128 MB) cover every split
+// count the planner picks.
+constexpr size_t kSplitWsFloats = size_t(32) << 20;
 // Workspace floats a split-K launch needs.
 inline size_t splitk_ws_floats(int M, int N, int splits) { return (size_t)splits * M * N; }
 // Slice count for `tiles` 128 x 128 output tiles of `kblocks` 64-wide K blocks on `sms` SMs: the S
@@ -100,6 +103,46 @@ cudaError_t gemm_prepare_device();
 constexpr int kGemmPair = 512;
 // Co-resident CTA pairs of the pair kernel on the current device (set by gemm_prepare_device).
 int gemm_pair_clusters();
+
+// K-block times credited to a split whose reduce kernel absorbs the LayerNorm that follows the GEMM:
+// the split costs the partials' round trip and the reduce (kSplitReduceBlocks) but saves the
+// LayerNorm launch, leaving about 8. Measured at 512 rows (ModernBERT-large, one B200): the attention
+// out-projection then splits 4 ways with the MLP LayerNorm in its reduce, 1.774 -> 1.687 ms per pass.
+constexpr int kSplitLnCredit = 20;
+
+// Tile and K split of one GEMM launch (host-only). Tile: the CTA-pair 256 x 256 tile when its tile
+// count fills every co-resident pair twice, else the one-CTA width (128 or 256) with fewer whole
+// waves, a 128 x 256 tile counting 1.6 of a 128 x 128 one (it reads each A block once per 256
+// columns: at 512 rows the GeGLU GEMM runs one wave of 84 wide tiles in 13 us against two waves of
+// 164 narrow ones in 17 us). K split (128-wide tiles only, when allowed): splitk_choose, with
+// `ln_credit` when the reduce kernel can absorb the following LayerNorm, and no more slices than a
+// workspace of `ws_floats` partials holds. nseg: K segments per K block (1 bf16, 3 fp32 parity).
+struct GemmPlan {
+  int bn = 128;
+  int splits = 1;
+};
+inline GemmPlan gemm_plan(int M, int N, int K, int nseg, int num_sms, int pair_clusters, bool allow_split,
+                          size_t ws_floats, int ln_credit) {
+  GemmPlan p;
+  if (N >= 256) {
+    const long long tp = (long long)((M + 255) / 256) * ((N + 255) / 256);
+    if (pair_clusters > 0 && tp >= 2LL * pair_clusters) {
+      p.bn = kGemmPair;
+    } else {
+      const long long rows = (M + 127) / 128;
+      const long long w128 = (rows * ((N + 127) / 128) + num_sms - 1) / num_sms;
+      const long long w256 = (rows * ((N + 255) / 256) + num_sms - 1) / num_sms;
+      p.bn = 10 * w128 > 16 * w256 ? 256 : 128;
+    }
+  }
+  if (p.bn == 128 && allow_split) {
+    const int tiles = ((M + 127) / 128) * ((N + 127) / 128);
+    int s = splitk_choose(tiles, ((K + 63) / 64) * nseg, num_sms, ln_credit);
+    while (s > 1 && splitk_ws_floats(M, N, s) > ws_floats) --s;
+    p.splits = s;
+  }
+  return p;
+}
 
 // `grid_ctas` caps the persistent grid (CTAs; a pair counts as two).
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, int bn,

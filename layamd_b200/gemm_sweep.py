@@ -32,18 +32,13 @@ def peaks():
         return 1400.0, 1590.0
 
 
-def pick_tile(M, N, sms):
-    """The engine's rule (engine.cpp Replica::pick_tile): the CTA-pair 256 x 256 tile when its tiles
-    fill every co-resident pair twice, else the width with fewer whole waves, a 128 x 256 tile
-    counting 1.6 of a 128 x 128 one."""
-    if N < 256:
-        return 128
-    if ((M + 255) // 256) * ((N + 255) // 256) >= 2 * (sms // 2):
-        return 512
-    rows = (M + 127) // 128
-    w128 = (rows * ((N + 127) // 128) + sms - 1) // sms
-    w256 = (rows * ((N + 255) // 256) + sms - 1) // sms
-    return 256 if 10 * w128 > 16 * w256 else 128
+def pick_tile(L, M, N, K, sms):
+    """The engine's tile for this shape (laya_plan_gemm: the CTA-pair 256 x 256 tile when its tiles
+    fill every co-resident pair twice, else the width with fewer whole waves); this sweep never splits
+    K, so only the tile is taken."""
+    bn, splits = ctypes.c_int(0), ctypes.c_int(0)
+    assert L.laya_plan_gemm(M, N, K, 0, sms, sms // 2, 0, ctypes.byref(bn), ctypes.byref(splits)) == 0
+    return bn.value
 
 
 def interleave_geglu(W, I):
@@ -87,7 +82,7 @@ def main():
             if epi == EPI["geglu"]:
                 W32 = interleave_geglu(W32, I)
             ncols = I if epi == EPI["geglu"] else N
-            bn = pick_tile(M, N, sms) if a.tile == "auto" else TILES[a.tile]
+            bn = pick_tile(L, M, N, K, sms) if a.tile == "auto" else TILES[a.tile]
             pos = torch.randint(0, 512, (M,), device=dev, dtype=torch.int32, generator=g)
             cos = torch.rand(512, 32, device=dev)
             sin = torch.rand(512, 32, device=dev)

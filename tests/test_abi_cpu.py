@@ -1,6 +1,7 @@
 """Host-side checks that need no GPU: the library loads and exports every symbol include/laya_api.h
 declares, the load-error path, and the pass packer against a restatement of the reference's packing
-rule (src/engine.hip:489-505) including the -1 validation contract."""
+rule (src/engine.hip:489-505) including the -1 validation contract, and the GEMM planner's choices at
+the measured shapes."""
 import ctypes
 import os
 import re
@@ -96,3 +97,38 @@ def test_packer_rejects_invalid_batches():
                 dict(ok, markers=[1, 10, 0, 5, 19]), dict(ok, markers=[1, 2, 0, 5, -1]),
                 dict(lens=[300], nmark=[256], markers=[1] * 256)]:
         assert run_plan(512, 1024, 128, **bad)[0] == -1
+
+
+def plan(L, M, N, K, parity=0, ln=0, sms=148, pairs=74):
+    bn, splits = ctypes.c_int(0), ctypes.c_int(0)
+    assert L.laya_plan_gemm(M, N, K, parity, sms, pairs, ln, ctypes.byref(bn), ctypes.byref(splits)) == 0
+    return bn.value, splits.value
+
+
+def test_gemm_planner_at_the_measured_shapes():
+    """The engine's per-launch GEMM plan (tile, K slices) on a 148-SM B200 with 74 co-resident CTA
+    pairs, at the ModernBERT-large shapes whose choices were measured: 512 rows (batch 1) and the
+    52,287-row C2 pass."""
+    L = load_lib()
+    # batch 1, 512 rows: QKV and K = 1024 stores stay whole on 128 x 128 tiles; GeGLU takes one wave
+    # of 128 x 256 tiles; the residual GEMMs followed by a bias-free LayerNorm split 4 ways (their
+    # reduce kernel takes the LayerNorm over), as does the head's K = 4096 FFN-2 (bias LayerNorm: no
+    # credit, still worth 4 slices)
+    assert plan(L, 512, 3072, 1024) == (128, 1)
+    assert plan(L, 512, 5248, 1024) == (256, 1)
+    assert plan(L, 512, 1024, 1024, ln=1) == (128, 4)
+    assert plan(L, 512, 1024, 2624, ln=1) == (128, 4)
+    assert plan(L, 512, 1024, 4096) == (128, 4)
+    # without the LayerNorm credit the K = 1024 residual GEMM stays whole
+    assert plan(L, 512, 1024, 1024) == (128, 1)
+    # fp32-parity mode: three products per K block make the K loops long enough to split without it
+    assert plan(L, 512, 1024, 1024, parity=1) == (128, 4)
+    # C2 pass: every encoder GEMM on CTA-pair 256 x 256 tiles, whole K
+    for N, K in ((3072, 1024), (1024, 1024), (5248, 1024), (1024, 2624)):
+        assert plan(L, 52287, N, K, ln=1) == (512, 1)
+    # 4096 rows: too few 256 x 256 tiles to fill the pairs twice, so one-CTA tiles by whole waves
+    assert plan(L, 4096, 1024, 1024) == (256, 1)
+    assert plan(L, 52287, 1024, 1024, pairs=0) == (256, 1)  # no pair kernel on the device
+    # bad arguments
+    bn, splits = ctypes.c_int(0), ctypes.c_int(0)
+    assert L.laya_plan_gemm(0, 1024, 1024, 0, 148, 74, 0, ctypes.byref(bn), ctypes.byref(splits)) == -1
