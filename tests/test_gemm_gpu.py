@@ -175,6 +175,34 @@ def test_geglu(L, I, bn):
     assert rel(out, ref) < 1e-4
 
 
+def test_geglu_gelu_error_bound(L):
+    """The epilogue's GELU (Abramowitz & Stegun 7.1.26 form of erfc, one reciprocal and one 2^x)
+    against the exact-erf GELU in fp64, isolated: A row m is s_m e_0 (s_m a power of two) and the
+    interleaved weight rows put x_n in column 0 of input row n and 1 in column 0 of its gate row, so
+    the accumulator holds y = s_m x_n and the gate s_m exactly; out / s_m = gelu(y) as computed by the
+    kernel, for |y| up to 12 on a dense bf16 grid. Bound: 1e-6 absolute plus 2^-22 relative (fp32
+    rounding of y * Phi(y) near |y| = 12 alone is up to 4.8e-7)."""
+    I, K = 2624, 64
+    xs = torch.linspace(-1.5, 1.5, I, device="cuda").bfloat16()
+    scales = [2.0 ** e for e in range(-4, 4)]
+    M = len(scales)
+    A = torch.zeros(M, K, device="cuda")
+    for m, sc in enumerate(scales):
+        A[m, 0] = sc
+    A = A.bfloat16()
+    W = torch.zeros(2 * I, K, device="cuda")
+    W[:I, 0] = xs.float()
+    W[I:, 0] = 1.0
+    W = W.bfloat16()
+    out = torch.empty((M, I), device="cuda")
+    gemm(L, A, interleave_geglu(W, I), out, M, 2 * I, K, epi=EPI_GEGLU, geglu_I=I, bn=256)
+    sc = torch.tensor(scales, device="cuda", dtype=torch.float64)[:, None]
+    y = sc * xs.double()[None, :]
+    ref = 0.5 * y * (1.0 + torch.erf(y / math.sqrt(2.0)))
+    err = (out.double() / sc - ref).abs()
+    assert float((err - (1e-6 + 2.0 ** -22 * ref.abs())).max()) <= 0.0, float(err.max())
+
+
 # ---------------------------------------------------------------- split-K (small M)
 @pytest.fixture(scope="module")
 def LS(L):
