@@ -7,6 +7,8 @@ use it, and only as the checker or the timed CPU baseline, never as a compute pa
 Contents:
   model           numpy fp32 restatement of the reference forward pass (ref/rl_common.py
                   DecisionModel + transformers ModernBertModel), per-layer capture included
+  ref_tools       builds the reference's own C++ host tools (src/bench_engine.cpp,
+                  src/test_parity.cpp), unmodified, against this library into oracle/_ref
 
 The seeded checkpoints and inputs it is run on come from ``layamd_b200.synthetic`` (input
 generators, shared with the benchmarks; they compute nothing of the model).
