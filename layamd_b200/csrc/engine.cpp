@@ -530,15 +530,21 @@ class Replica {
     }
     staged_prof_events.clear();
   }
+  // adds one timed launch of stage `name` to the profile table
+  void prof_add(const char* name, float ms) {
+    for (auto& kv : prof_acc)
+      if (kv.first == name) {
+        kv.second.first += ms;
+        kv.second.second += 1;
+        return;
+      }
+    prof_acc.push_back({name, {(double)ms, 1}});
+  }
   void prof_collect() {
     for (auto& t : prof_pending) {
       float ms = 0.f;
       cudaEventElapsedTime(&ms, std::get<1>(t), std::get<2>(t));
-      const std::string n = std::get<0>(t);
-      bool found = false;
-      for (auto& kv : prof_acc)
-        if (kv.first == n) { kv.second.first += ms; kv.second.second += 1; found = true; break; }
-      if (!found) prof_acc.push_back({n, {(double)ms, 1}});
+      prof_add(std::get<0>(t), ms);
     }
     prof_pending.clear();
     ev_used = 0;
@@ -1023,11 +1029,7 @@ class Replica {
     for (auto& t : staged_prof_events) {
       float ms = 0.f;
       if (cudaEventElapsedTime(&ms, std::get<1>(t), std::get<2>(t)) != cudaSuccess) return -2;
-      const std::string n = std::get<0>(t);
-      bool found = false;
-      for (auto& kv : prof_acc)
-        if (kv.first == n) { kv.second.first += ms; kv.second.second += 1; found = true; break; }
-      if (!found) prof_acc.push_back({n, {(double)ms, 1}});
+      prof_add(std::get<0>(t), ms);
     }
     int herr = 0;
     cudaMemcpy(&herr, d_err, 4, cudaMemcpyDeviceToHost);
