@@ -95,8 +95,13 @@ int laya_plan_gemm(int M, int N, int K, int parity, int num_sms, int pair_cluste
                    int* splits);
 
 /* The replica (0..ndev-1) each of B questions goes to when a call is sharded over ndev GPUs, as
- * laya_forward_batch does it; host-only. Returns 0 or -1. */
-int laya_shard_plan(int ndev, int B, const int* lens, int* owner);
+ * laya_forward_batch does it, for a model of hidden size d, GeGLU width `intermediate`, n_layers
+ * encoder layers of which n_global use global attention, sliding window `window` (full width) and a
+ * head FFN of 4d; host-only. Longest processing time first on each question's modelled device time
+ * (its algorithmic FLOPs for length lens[b] and nmark[b] options, attention FLOPs weighted by their
+ * measured cost relative to GEMM FLOPs) onto the least-loaded replica. Returns 0 or -1. */
+int laya_shard_plan(int ndev, int B, const int* lens, const int* nmark, int d, int intermediate, int n_layers,
+                    int n_global, int window, int* owner);
 
 /* Benchmark support: validates, packs and uploads one batch (it must fit one pass per device) and
  * keeps it resident; laya_replay then runs the staged pass `iters` times back to back on every
@@ -131,13 +136,15 @@ int laya_set_dump_dir(void* h, const char* dir);
  * add into resid[M][N]. out_mode: 0 bf16, 1 bf16 hi/lo planes, 2 fp32. act: 0 none, 1 ReLU, 2 GELU.
  * bn: 128 or 256 (one CTA per 128 x bn tile) or 512 (a CTA pair per 256 x 256 tile, 2-SM MMA).
  * planes 2 selects the three-product fp32 emulation. stream may be NULL. With
- * sync != 0 the call waits for the GPU and returns -100-code if the kernel reported an error. */
+ * sync != 0 the call waits for the GPU and returns -100-code if a kernel reported an error (this
+ * call's, or one left unread by an earlier call with sync = 0: see laya_b200_kernel_error). */
 int laya_b200_gemm(const void* A, const void* W, void* out, float* resid, const float* bias, int M, int N, int K,
                    int planes, int epi, int out_mode, int act, int bn, const float* cos_t, const float* sin_t,
                    const int* pos, int rope_cols, int geglu_I, void* stream, int sync);
 
-/* laya_b200_gemm with the K loop split into `splits` slices (1..8) run by different CTAs, for small M
- * where the output tiles alone cannot fill the GPU (one-CTA tiles, bn 128 or 256). The fp32 partials
+/* laya_b200_gemm with the K loop split into `splits` slices (1..8, and at most one per 64-wide K
+ * block: ceil(K / 64), x3 in parity mode; else -2) run by different CTAs, for small M where the
+ * output tiles alone cannot fill the GPU (one-CTA tiles, bn 128 or 256). The fp32 partials
  * go to a workspace the library allocates on the device and keeps for later calls; a second kernel
  * sums them in slice order and applies the epilogue, so results do not depend on scheduling. Calls
  * that overlap on the GPU (other streams) share that workspace and must not be issued. */
@@ -160,9 +167,23 @@ int laya_b200_attention(const void* qkv, void* out, int rows, int B, const int* 
  * the bounded wait that every pipeline kernel of this library uses on its mbarriers: one thread waits
  * on a barrier phase that nothing completes, gives up after the wait budget (about 2^31 SM cycles,
  * roughly one second), records its error code in a device word and returns, so the kernel ends
- * normally and the context stays usable. Writes the recorded code (30) to *code, the wait's length in
- * SM cycles to *cycles and the kernel's device time to *ms. Returns 0, or -2 if a CUDA call failed. */
+ * normally and the context stays usable. The word is the one the kernel-level entry points share
+ * (see laya_b200_kernel_error), and the code stays there until it is read. Writes the recorded code
+ * (30) to *code, the wait's length in SM cycles to *cycles and the kernel's device time to *ms.
+ * Returns 0, -2 if a CUDA call failed, or -3 without launching when that word already holds an
+ * earlier, unread code. */
 int laya_b200_watchdog_selftest(int device, int* code, long long* cycles, float* ms);
+
+/* No counterpart in the reference. Kernel errors of the kernel-level entry points on GPU `device`
+ * (laya_b200_gemm, laya_b200_gemm_splitk, laya_b200_gemm_splitk_noalloc, laya_b200_attention, the
+ * watchdog self-test). A kernel whose bounded wait ran out records a code in a device word (the first
+ * code wins) and ends; a call with sync != 0 reports it as -100-code, but a call with sync = 0 cannot,
+ * so the word keeps the code until it is read: by the next call with sync != 0 on the same word, or by
+ * this function. It waits for all work on the device, reads and clears both words (the one the
+ * allocating entries share and the one in the allocation-free entry's static array) and returns the
+ * first code found (GEMM 1-5, attention 16-18, self-test 30), 0 if none, -1 for a bad device
+ * ordinal, -2 if a CUDA call failed. It allocates nothing. */
+int laya_b200_kernel_error(int device);
 
 /* No counterpart in the reference. laya_b200_gemm_splitk for callers that cannot allocate device
  * memory: a host whose memory manager reserves the GPU's memory up front (a serving stack with a
@@ -174,8 +195,10 @@ int laya_b200_watchdog_selftest(int device, int* code, long long* cycles, float*
  * without launching. The first call on a device sets up
  * (kernel attributes and the array's device address, no allocation); make it before any stream
  * capture. Every call on a device shares the array: calls that overlap on the GPU (other streams,
- * other threads) race and must not be issued. Each call clears the error word it inherits from the
- * previous one; every slice overwrites its whole plane of partials. */
+ * other threads) race and must not be issued. Every slice overwrites its whole plane of partials
+ * (splits may not exceed the K blocks, ceil(K / 64) x 3 in parity mode, else -2), so no call sees
+ * another's partials. The error word in the array is zeroed at set-up and then kept: a code left by
+ * a call with sync = 0 is reported by the next call with sync != 0 or by laya_b200_kernel_error. */
 int laya_b200_gemm_splitk_noalloc(const void* A, const void* W, void* out, float* resid, const float* bias, int M,
                                   int N, int K, int planes, int epi, int out_mode, int act, int bn,
                                   const float* cos_t, const float* sin_t, const int* pos, int rope_cols,

@@ -52,7 +52,7 @@ def load_lib(path: str = LIB_PATH) -> ctypes.CDLL:
         "laya_prof_get": (i, [vp, ctypes.c_char_p, ctypes.POINTER(d), ctypes.POINTER(ctypes.c_longlong)]),
         "laya_plan_passes": (i, [vp, i, _IP, _IP, _IP, i, _IP, _IP, _IP]),
         "laya_plan_passes_cfg": (i, [i, i, i, i, _IP, _IP, _IP, i, _IP, _IP, _IP]),
-        "laya_shard_plan": (i, [i, i, _IP, _IP]),
+        "laya_shard_plan": (i, [i, i, _IP, _IP, i, i, i, i, i, _IP]),
         "laya_stage": (i, [vp, i, _IP, _IP, _IP, _IP, _IP]),
         "laya_replay": (i, [vp, i, ctypes.POINTER(d)]),
         "laya_replay_profiled": (i, [vp, i]),
@@ -66,6 +66,7 @@ def load_lib(path: str = LIB_PATH) -> ctypes.CDLL:
         "laya_b200_gemm_splitk": (i, [vp, vp, vp, vp, vp, i, i, i, i, i, i, i, i, vp, vp, vp, i, i, i, vp, i]),
         "laya_b200_attention": (i, [vp, vp, i, i, _IP, i, i, i, vp, i]),
         "laya_b200_gemm_splitk_noalloc": (i, [vp, vp, vp, vp, vp, i, i, i, i, i, i, i, i, vp, vp, vp, i, i, i, vp, i]),
+        "laya_b200_kernel_error": (i, [i]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -108,9 +108,19 @@ int laya_plan_passes(void* h, int B, const int* lens, const int* nmark, const in
   return (int)plans.size();
 }
 
-int laya_shard_plan(int ndev, int B, const int* lens, int* owner) {
-  if (ndev < 1 || B < 0 || (B > 0 && (!lens || !owner))) return -1;
-  laya::shard_owners(B, lens, ndev, owner);
+int laya_shard_plan(int ndev, int B, const int* lens, const int* nmark, int d, int intermediate, int n_layers,
+                    int n_global, int window, int* owner) {
+  if (ndev < 1 || B < 0 || (B > 0 && (!lens || !nmark || !owner)) || d <= 0 || intermediate <= 0 || n_layers <= 0 ||
+      n_global < 0 || n_global > n_layers || window < 0)
+    return -1;
+  laya::ShardModel m;
+  m.d = d;
+  m.intermediate = intermediate;
+  m.head_ffn = 4LL * d;
+  m.n_layers = n_layers;
+  m.n_global = n_global;
+  m.window = window;
+  laya::shard_owners(B, lens, nmark, ndev, m, owner);
   return 0;
 }
 

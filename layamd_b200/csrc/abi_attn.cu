@@ -13,7 +13,6 @@ namespace {
 std::mutex g_mu;
 struct AttnDev {
   bool ready = false;
-  int* err = nullptr;      // device error word
   int* ticket = nullptr;   // work / exit counters of the persistent tcgen05 kernel (kept zero between launches)
   int* meta = nullptr;     // soff[B] | slen[B] | items (4 ints each)
   size_t meta_ints = 0;
@@ -56,10 +55,8 @@ extern "C" int laya_b200_attention(const void* qkv, void* out, int rows, int B, 
     AttnDev& d = g_dev[dev];
     if (!d.ready) {
       if (attn_tc_prepare_device() != cudaSuccess) return -4;
-      if (cudaMalloc(&d.err, sizeof(int)) != cudaSuccess) return -4;
       if (cudaMalloc(&d.ticket, 2 * sizeof(int)) != cudaSuccess) return -4;
       if (cudaMemset(d.ticket, 0, 2 * sizeof(int)) != cudaSuccess) return -4;
-      if (cudaMemset(d.err, 0, sizeof(int)) != cudaSuccess) return -4;
       d.ready = true;
     }
     if (d.meta_ints < n_ints) {
@@ -70,9 +67,10 @@ extern "C" int laya_b200_attention(const void* qkv, void* out, int rows, int B, 
       d.meta_ints = n_ints;
     }
     d_meta = d.meta;
-    err = d.err;
     ticket = d.ticket;
   }
+  err = entry_error_word(dev);
+  if (!err) return -4;
   // the previous call may still read the metadata block: order the upload after it on the stream
   if (cudaMemcpyAsync(d_meta, meta.data(), meta.size() * sizeof(int), cudaMemcpyHostToDevice, st) != cudaSuccess ||
       cudaMemcpyAsync(d_meta + meta.size(), items.data(), items.size() * sizeof(AttnItem), cudaMemcpyHostToDevice,
@@ -114,6 +112,8 @@ extern "C" int laya_b200_attention(const void* qkv, void* out, int rows, int B, 
     cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost);
     if (h) {
       cudaMemset(err, 0, sizeof(int));
+      // an aborted launch can leave the work / exit counters part-way: clear them for the next call
+      cudaMemset(ticket, 0, 2 * sizeof(int));
       return -100 - h;
     }
   }

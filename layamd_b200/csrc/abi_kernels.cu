@@ -9,9 +9,12 @@
 #include "laya_api.h"
 
 namespace {
+std::mutex g_err_mu;
+std::vector<int*> g_err_word;  // per device: the error word of the kernel-level entry points
+
 std::mutex g_mu;
 struct DevState {
-  int* err = nullptr;        // device error word
+  bool ready = false;
   float* ws = nullptr;       // split-K partials (grown on demand)
   size_t ws_floats = 0;
 };
@@ -20,12 +23,36 @@ std::vector<DevState> g_dev;
 DevState* dev_state(int dev) {
   if ((int)g_dev.size() <= dev) g_dev.resize(dev + 1);
   DevState& d = g_dev[dev];
-  if (!d.err) {
+  if (!d.ready) {
     if (laya::gemm_prepare_device() != cudaSuccess) return nullptr;
-    if (cudaMalloc(&d.err, sizeof(int)) != cudaSuccess) return nullptr;
-    cudaMemset(d.err, 0, sizeof(int));
+    d.ready = true;
   }
   return &d;
+}
+}  // namespace
+
+namespace laya {
+int* entry_error_word(int dev) {
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  if (dev < 0) return nullptr;
+  if ((int)g_err_word.size() <= dev) g_err_word.resize(dev + 1, nullptr);
+  if (!g_err_word[dev]) {
+    int* p = nullptr;
+    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
+    if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) {
+      cudaFree(p);
+      return nullptr;
+    }
+    g_err_word[dev] = p;
+  }
+  return g_err_word[dev];
+}
+}  // namespace laya
+
+namespace {
+int* existing_error_word(int dev) {
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  return dev >= 0 && dev < (int)g_err_word.size() ? g_err_word[dev] : nullptr;
 }
 int num_sms(int dev) {
   int n = 0;
@@ -40,6 +67,8 @@ int run_gemm(const void* A, const void* W, void* out, float* resid, const float*
   using namespace laya;
   if ((planes != 1 && planes != 2) || M <= 0 || N <= 0 || K <= 0) return -2;
   if (bn != 128 && bn != 256 && bn != kGemmPair) return -2;
+  // at most one K slice per 64-wide K block (of every product segment in parity mode)
+  if (splits > ((K + 63) / 64) * (planes == 2 ? 3 : 1)) return -2;
   CUtensorMap ta, tb, tc;
   if (!make_operand_map(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)planes, 128)) return -3;
   const uint32_t box_b = bn == kGemmPair ? 128u : static_cast<uint32_t>(bn);  // a pair tile loads 128 B rows per CTA
@@ -89,12 +118,11 @@ extern "C" int laya_b200_gemm(const void* A, const void* W, void* out, float* re
                               int geglu_I, void* stream, int sync) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;
-  int* err;
+  int* err = laya::entry_error_word(dev);
+  if (!err) return -4;
   {
     std::lock_guard<std::mutex> lk(g_mu);
-    DevState* d = dev_state(dev);
-    if (!d) return -4;
-    err = d->err;
+    if (!dev_state(dev)) return -4;
   }
   return run_gemm(A, W, out, resid, bias, M, N, K, planes, epi, out_mode, act, bn, cos_t, sin_t, pos, rope_cols,
                   geglu_I, stream, sync, 1, nullptr, err, dev);
@@ -109,12 +137,12 @@ extern "C" int laya_b200_gemm_splitk(const void* A, const void* W, void* out, fl
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;
   if (splits < 1 || splits > kMaxSplits || (splits > 1 && bn == kGemmPair) || M <= 0 || N <= 0) return -2;
   float* ws = nullptr;
-  int* err;
+  int* err = entry_error_word(dev);
+  if (!err) return -4;
   {
     std::lock_guard<std::mutex> lk(g_mu);
     DevState* d = dev_state(dev);
     if (!d) return -4;
-    err = d->err;
     const size_t need_ws = splitk_ws_floats(M, N, splits);
     if (splits > 1 && d->ws_floats < need_ws) {
       if (d->ws) cudaFree(d->ws);
@@ -152,7 +180,7 @@ std::mutex g_noalloc_mu;
 unsigned char* g_noalloc_base[kNoAllocMaxDevices];  // device address of g_noalloc_scratch, per device
 
 // Set-up on the first call on a device (with that device current): the kernels' shared-memory
-// limits and the array's device address. Neither allocates.
+// limits, the array's device address and a zero error word. None of it allocates.
 unsigned char* noalloc_scratch(int dev) {
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (!g_noalloc_base[dev]) {
@@ -168,9 +196,21 @@ unsigned char* noalloc_scratch(int dev) {
               cudaGetErrorString(e));
       return nullptr;
     }
+    // the error word starts at zero once; after that it keeps a kernel's code until a call with
+    // sync != 0 or laya_b200_kernel_error reads it
+    e = cudaMemset(static_cast<unsigned char*>(p) + kNoAllocWsBytes, 0, sizeof(int));
+    if (e != cudaSuccess) {
+      fprintf(stderr, "[laya] gemm_noalloc: clearing the error word on device %d failed: %s\n", dev,
+              cudaGetErrorString(e));
+      return nullptr;
+    }
     g_noalloc_base[dev] = static_cast<unsigned char*>(p);
   }
   return g_noalloc_base[dev];
+}
+unsigned char* noalloc_scratch_if_set_up(int dev) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  return dev >= 0 && dev < kNoAllocMaxDevices ? g_noalloc_base[dev] : nullptr;
 }
 }  // namespace
 
@@ -195,10 +235,37 @@ extern "C" int laya_b200_gemm_splitk_noalloc(const void* A, const void* W, void*
   if (!base) return -4;
   float* ws = reinterpret_cast<float*>(base);
   int* err = reinterpret_cast<int*>(base + kNoAllocWsBytes);
-  // The array keeps whatever the last call (possibly an aborted one) left: the error word starts
-  // every call at zero. The partials need no clearing: every slice overwrites its whole plane.
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess) return -5;
+  // The array keeps whatever the last call left. The partials need no clearing: run_gemm gives every
+  // slice at least one K block, so every slice overwrites its whole plane. The error word is not
+  // cleared here, so that a code an earlier call with sync = 0 left is reported, not lost.
   return run_gemm(A, W, out, resid, bias, M, N, K, planes, epi, out_mode, act, bn, cos_t, sin_t, pos, rope_cols,
                   geglu_I, stream, sync, splits, ws, err, dev);
+}
+
+// ---------------------------------------------------------------- asynchronous error reports
+extern "C" int laya_b200_kernel_error(int device) {
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return -1;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (cudaSetDevice(device) != cudaSuccess) return -1;
+  int code = 0;
+  int rc = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) rc = -2;
+  int* words[2] = {existing_error_word(device), nullptr};
+  if (unsigned char* base = noalloc_scratch_if_set_up(device)) words[1] = reinterpret_cast<int*>(base + kNoAllocWsBytes);
+  for (int* w : words) {
+    if (!w || rc) continue;
+    int h = 0;
+    if (cudaMemcpy(&h, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+      rc = -2;
+      break;
+    }
+    if (h) {
+      if (!code) code = h;
+      if (cudaMemset(w, 0, sizeof(int)) != cudaSuccess) rc = -2;
+    }
+  }
+  cudaSetDevice(prev);
+  return rc ? rc : code;
 }

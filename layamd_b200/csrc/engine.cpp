@@ -191,6 +191,10 @@ class Replica {
   std::vector<std::tuple<const char*, cudaEvent_t, cudaEvent_t>> staged_prof_events;
   bool capturing_prof = false;
 
+  // Failure injection for host-side tests (LAYA_FAIL_REPLICA=i[:n] at load): this replica's next
+  // n non-empty shards return -2 before anything is uploaded or launched.
+  int fail_runs = 0;
+
   Replica(Engine& e, int d) : E(e), cfg(e.cfg), dev(d) {}
   ~Replica() { release(); }
 
@@ -649,7 +653,7 @@ class Replica {
     launched(attn_tc_launch(qkv_map, qkv_map64, a, d_attn_ticket, d_err, st));
   }
 
-  bool dumping() const { return !E.dump_dir.empty() && !capturing && dev == E.reps[0]->dev; }
+  bool dumping() const { return !E.dump_dir.empty() && !capturing && this == E.reps[0].get(); }
   void dump(const char* name, const float* src, int rows) {
     if (!dumping()) return;
     std::vector<float> h((size_t)rows * cfg.d);
@@ -918,6 +922,11 @@ class Replica {
   // Runs every question of `qs` (this replica's shard) through as many passes as needed.
   int run(const std::vector<Question>& qs) {
     if (qs.empty()) return 0;
+    if (fail_runs > 0) {
+      --fail_runs;
+      fprintf(stderr, "[laya] device %d: injected failure (LAYA_FAIL_REPLICA), nothing launched\n", dev);
+      return -2;
+    }
     if (cudaSetDevice(dev) != cudaSuccess) return -2;
     std::vector<int> lens(qs.size()), nms(qs.size());
     for (size_t i = 0; i < qs.size(); ++i) { lens[i] = qs[i].len; nms[i] = qs[i].nmark; }
@@ -1050,7 +1059,10 @@ class Replica {
 
 // ===================================================================== Engine
 Engine::Engine() = default;
-Engine::~Engine() { reps.clear(); }
+Engine::~Engine() {
+  reps.clear();
+  workers.clear();
+}
 
 bool Engine::load(const std::string& dir, int prec, const std::string& devices, std::string* err) {
   try {
@@ -1104,21 +1116,138 @@ bool Engine::load(const std::string& dir, int prec, const std::string& devices, 
   std::vector<std::string> errs(devs.size());
   std::vector<int> ok(devs.size(), 0);
   for (int d : devs) reps.emplace_back(new Replica(*this, d));
-  std::vector<std::thread> th;
-  for (size_t i = 0; i < devs.size(); ++i)
-    th.emplace_back([&, i] { ok[i] = reps[i]->load(W, &errs[i]) ? 1 : 0; });
-  for (auto& t : th) t.join();
+  workers.resize(devs.size());
+  for (size_t i = 1; i < devs.size(); ++i) workers[i].reset(new Worker());
+  each_replica([&](size_t i) {
+    ok[i] = reps[i]->load(W, &errs[i]) ? 1 : 0;
+    return 0;
+  });
   cudaSetDevice(prev);
   for (size_t i = 0; i < devs.size(); ++i)
     if (!ok[i]) { *err = "device " + std::to_string(devs[i]) + ": " + errs[i]; return false; }
+  if (const char* f = getenv("LAYA_FAIL_REPLICA")) {
+    const int i = atoi(f);
+    const char* c = strchr(f, ':');
+    if (i >= 0 && i < (int)reps.size()) reps[i]->fail_runs = c ? atoi(c + 1) : 1;
+  }
   if (getenv("LAYA_VERBOSE"))
     printf("[laya] ready: %zu device(s) max_tokens/pass=%d graphs=%d precision=%s\n", reps.size(), pass_tokens,
            (int)use_graphs, precision ? "fp32parity" : "bf16");
   return true;
 }
 
-// Longest-processing-time-first assignment of questions to replicas on their length, keeping the
-// input order inside each shard.
+// ===================================================================== workers
+Worker::Worker() : th_([this] { loop(); }) {}
+
+Worker::~Worker() {
+  {
+    std::lock_guard<std::mutex> lk(mu_);
+    stop_ = true;
+  }
+  cv_.notify_all();
+  th_.join();
+}
+
+void Worker::post(std::function<int()> job) {
+  {
+    std::lock_guard<std::mutex> lk(mu_);
+    job_ = std::move(job);
+    has_job_ = true;
+    done_ = false;
+  }
+  cv_.notify_all();
+}
+
+int Worker::wait() {
+  std::unique_lock<std::mutex> lk(mu_);
+  cv_.wait(lk, [&] { return done_; });
+  done_ = false;
+  return rc_;
+}
+
+void Worker::loop() {
+  std::unique_lock<std::mutex> lk(mu_);
+  for (;;) {
+    cv_.wait(lk, [&] { return has_job_ || stop_; });
+    if (!has_job_) return;  // stop, nothing pending
+    std::function<int()> job = std::move(job_);
+    has_job_ = false;
+    lk.unlock();
+    int rc;
+    try {
+      rc = job();
+    } catch (...) {
+      rc = -2;
+    }
+    lk.lock();
+    rc_ = rc;
+    done_ = true;
+    cv_.notify_all();
+  }
+}
+
+int Engine::each_replica(const std::function<int(size_t)>& fn) {
+  const size_t G = reps.size();
+  for (size_t i = 1; i < G; ++i) workers[i]->post([&fn, i] { return fn(i); });
+  std::vector<int> rc(G, 0);
+  try {
+    rc[0] = fn(0);
+  } catch (...) {
+    rc[0] = -2;
+  }
+  for (size_t i = 1; i < G; ++i) rc[i] = workers[i]->wait();  // every worker finishes before the call returns
+  for (int r : rc)
+    if (r) return r;
+  return 0;
+}
+
+// ===================================================================== request sharding
+ShardModel shard_model(const Config& c) {
+  ShardModel m;
+  m.d = c.d;
+  m.intermediate = c.intermediate;
+  m.head_ffn = c.head_ffn > 0 ? c.head_ffn : 4LL * c.d;
+  m.n_layers = c.n_layers;
+  m.n_global = 0;
+  for (int l = 0; l < c.n_layers && l < (int)c.layer_types.size(); ++l)
+    if (c.layer_types[l] == AttnKind::Global) ++m.n_global;
+  m.window = c.local_attention;
+  return m;
+}
+
+long long question_cost(const ShardModel& m, int L, int k) {
+  const long long D = m.d, I = m.intermediate, FF = m.head_ffn, NL = m.n_layers, ng = m.n_global;
+  const long long ns = NL - ng, h = m.window / 2, l = L, kk = k;
+  // keys inside |q - key| <= h summed over the queries of one sequence:
+  // sum_q min(L-1, q+h) - max(0, q-h) + 1, in closed form
+  const long long t = l > h ? l - h : 0, u = l - 1 - h > 0 ? l - 1 - h : 0;
+  const long long band = t * (t - 1) / 2 + t * h + (l - t) * (l - 1) - u * (u + 1) / 2 + l;
+  const long long gemm = 2 * l * (4 * D * D + 3 * I * D) * NL     // encoder: QKV, out, MLP-in (2I), MLP-out
+                         + 2 * l * (4 * D * D + 2 * D * FF)       // head layer 0 on every row
+                         + 2 * l * 3 * D * D                      // head layer 1: K, V (and Q) of every row
+                         + 2 * (kk + 1) * (D * D + 2 * D * FF)    // head layer 1 on the gathered rows
+                         + 2 * kk * D * D;                        // scorer
+  const long long glob = 4 * D * l * l * (ng + 1)                 // global layers and head layer 0
+                         + 4 * D * l * (kk + 1);                  // head layer 1, gathered queries
+  const long long slide = 4 * D * ns * band;
+  return 4 * gemm + 14 * glob + 26 * slide;
+}
+
+void shard_owners(int B, const int* lens, const int* nmark, int G, const ShardModel& m, int* owner) {
+  std::vector<long long> cost(B);
+  for (int b = 0; b < B; ++b) cost[b] = question_cost(m, lens[b], nmark[b]);
+  std::vector<int> order(B);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost[a] > cost[b]; });
+  std::vector<long long> load(G, 0);
+  for (int b : order) {
+    const int g = (int)(std::min_element(load.begin(), load.end()) - load.begin());
+    owner[b] = g;
+    load[g] += cost[b];
+  }
+}
+
+// Questions of each replica for one call (shard_owners), in input order inside each shard.
 std::vector<std::vector<Question>> Engine::shard(int B, const int* lens, const int* ids, const int* nmark,
                                                  const int* markers, const int* qtypes, float* logits, float* act) {
   const int G = (int)reps.size();
@@ -1135,21 +1264,9 @@ std::vector<std::vector<Question>> Engine::shard(int B, const int* lens, const i
     return out;
   }
   std::vector<int> owner(B);
-  shard_owners(B, lens, G, owner.data());
+  shard_owners(B, lens, nmark, G, shard_model(cfg), owner.data());
   for (int b = 0; b < B; ++b) out[owner[b]].push_back(all[b]);
   return out;
-}
-
-void shard_owners(int B, const int* lens, int G, int* owner) {
-  std::vector<int> order(B);
-  std::iota(order.begin(), order.end(), 0);
-  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return lens[a] > lens[b]; });
-  std::vector<long long> load(G, 0);
-  for (int b : order) {
-    const int g = (int)(std::min_element(load.begin(), load.end()) - load.begin());
-    owner[b] = g;
-    load[g] += lens[b] + 64;  // + per-question fixed cost
-  }
 }
 
 int Engine::forward_batch(int B, const int* lens, const int* ids, const int* nmark, const int* markers,
@@ -1158,14 +1275,7 @@ int Engine::forward_batch(int B, const int* lens, const int* ids, const int* nma
   if (B == 0) return 0;
   auto shards = shard(B, lens, ids, nmark, markers, qtypes, logits, act);
   if (reps.size() == 1) return reps[0]->run(shards[0]);
-  std::vector<int> rc(reps.size(), 0);
-  std::vector<std::thread> th;
-  for (size_t i = 1; i < reps.size(); ++i) th.emplace_back([&, i] { rc[i] = reps[i]->run(shards[i]); });
-  rc[0] = reps[0]->run(shards[0]);
-  for (auto& t : th) t.join();
-  for (int r : rc)
-    if (r) return r;
-  return 0;
+  return each_replica([&](size_t i) { return reps[i]->run(shards[i]); });
 }
 
 int Engine::stage(int B, const int* lens, const int* ids, const int* nmark, const int* markers, const int* qtypes) {
@@ -1183,35 +1293,18 @@ int Engine::stage(int B, const int* lens, const int* ids, const int* nmark, cons
   sink.assign(nk + (size_t)B * cfg.n_act + 1, 0.f);
   auto shards = shard(B, st_lens_.data(), st_ids_.data(), st_nmark_.data(), st_markers_.data(), st_qt_.data(),
                       sink.data(), sink.data() + nk);
-  std::vector<int> rc(reps.size(), 0);
-  std::vector<std::thread> th;
-  for (size_t i = 0; i < reps.size(); ++i) th.emplace_back([&, i] { rc[i] = reps[i]->stage_batch(shards[i]); });
-  for (auto& t : th) t.join();
-  for (int r : rc)
-    if (r) return r;
-  return 0;
+  return each_replica([&](size_t i) { return reps[i]->stage_batch(shards[i]); });
 }
 
 int Engine::replay(int iters, double* ms) {
-  std::vector<int> rc(reps.size(), 0);
   std::vector<double> t(reps.size(), 0.0);
-  std::vector<std::thread> th;
-  for (size_t i = 0; i < reps.size(); ++i) th.emplace_back([&, i] { rc[i] = reps[i]->replay(iters, &t[i]); });
-  for (auto& x : th) x.join();
+  const int rc = each_replica([&](size_t i) { return reps[i]->replay(iters, &t[i]); });
   *ms = *std::max_element(t.begin(), t.end());
-  for (int r : rc)
-    if (r) return r;
-  return 0;
+  return rc;
 }
 
 int Engine::replay_profiled(int iters) {
-  std::vector<int> rc(reps.size(), 0);
-  std::vector<std::thread> th;
-  for (size_t i = 0; i < reps.size(); ++i) th.emplace_back([&, i] { rc[i] = reps[i]->replay_profiled(iters); });
-  for (auto& x : th) x.join();
-  for (int r : rc)
-    if (r) return r;
-  return 0;
+  return each_replica([&](size_t i) { return reps[i]->replay_profiled(iters); });
 }
 
 int Engine::staged_results(float* logits, float* act) {

@@ -9,15 +9,19 @@
 //   * per-pass metadata staged in one pinned host block and uploaded with one copy; each pass shape
 //     (padded rows, questions, gathered rows) is captured once as a CUDA graph and replayed;
 //   * with several devices, each forward call shards its questions across the replicas (longest
-//     processing time first on the question length), each replica running the single-GPU path in
-//     its own host thread; no collective.
+//     processing time first on the question's modelled device time), each replica running the
+//     single-GPU path on its own long-lived host thread; no collective.
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <condition_variable>
+#include <functional>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
+#include <thread>
 #include <tuple>
 #include <vector>
 
@@ -45,9 +49,27 @@ bool plan_passes(int B, const int* lens, const int* nmark, int pass_tokens, int 
 // marker count in [1, 255], every marker inside its sequence.
 bool validate_batch(int B, const int* lens, const int* nmark, const int* markers, int max_len);
 
-// Replica of each question when a call is sharded over G replicas: longest question first onto the
-// least-loaded replica (load = length + 64 per question); ties keep input order.
-void shard_owners(int B, const int* lens, int G, int* owner);
+// Model dimensions the shard cost model needs (a subset of Config, so host-only callers can pass
+// them by value).
+struct ShardModel {
+  long long d = 1024, intermediate = 2624, head_ffn = 4096;
+  int n_layers = 28, n_global = 10, window = 128;  // window: full width, |q - k| <= window / 2
+};
+ShardModel shard_model(const Config& c);
+
+// Device cost of one question of length L with k options, in quarter-FLOPs at the encoder GEMMs' rate:
+// the algorithmic FLOPs of the forward pass (every GEMM of the encoder and both head layers, the
+// global and sliding attention, head-layer attention, the gathered rows of the last head layer and
+// the scorer), each term weighted by how long a FLOP of that kind takes on a B200 relative to a GEMM
+// FLOP. Measured on the C2 pass in bf16: GEMMs 1116 TFLOP/s, global attention 316, sliding attention
+// 175, so the weights are 4 (GEMM), 14 (global / head attention) and 26 (sliding attention) per FLOP.
+// Integer arithmetic, so that a restatement reproduces the assignment exactly.
+long long question_cost(const ShardModel& m, int L, int k);
+
+// Replica of each question when a call is sharded over G replicas: longest processing time first
+// (question_cost, descending; ties in input order) onto the least-loaded replica (lowest index on a
+// tie). Each replica then runs its questions in input order.
+void shard_owners(int B, const int* lens, const int* nmark, int G, const ShardModel& m, int* owner);
 
 struct Mat {  // a GEMM weight: planes x [N, K] bf16 with its TMA descriptors
   bf16* p = nullptr;
@@ -72,6 +94,26 @@ struct Question {  // one question of the caller's batch, by reference into the 
 
 class Replica;
 
+// A host thread that runs one job at a time for one replica, started at load and kept for the
+// handle's life, so a sharded call costs a hand-off instead of a thread start per replica.
+class Worker {
+ public:
+  Worker();
+  ~Worker();
+  Worker(const Worker&) = delete;
+  Worker& operator=(const Worker&) = delete;
+  void post(std::function<int()> job);  // the previous job must have been waited for
+  int wait();                           // blocks until the posted job returns; its result
+ private:
+  void loop();
+  std::mutex mu_;
+  std::condition_variable cv_;
+  std::function<int()> job_;
+  bool has_job_ = false, done_ = false, stop_ = false;
+  int rc_ = 0;
+  std::thread th_;
+};
+
 class Engine {
  public:
   Config cfg;
@@ -81,6 +123,8 @@ class Engine {
   bool prof_on = false;
   std::string dump_dir;
   std::vector<std::unique_ptr<Replica>> reps;
+  // workers[i] runs replica i's part of a call for i >= 1; replica 0 runs on the caller's thread
+  std::vector<std::unique_ptr<Worker>> workers;
 
   Engine();
   ~Engine();
@@ -103,6 +147,9 @@ class Engine {
   // staged batch for laya_stage / laya_replay
   std::vector<int> st_lens_, st_ids_, st_nmark_, st_markers_, st_qt_;
   int st_B_ = 0;
+  // Runs fn(i) for every replica i at once (replica 0 on the calling thread, the others on their
+  // workers), waits for all of them and returns the first non-zero result in replica order.
+  int each_replica(const std::function<int(size_t)>& fn);
   std::vector<std::vector<Question>> shard(int B, const int* lens, const int* ids, const int* nmark,
                                            const int* markers, const int* qtypes, float* logits, float* act);
 };

@@ -840,6 +840,9 @@ cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
                         (ep.out_mode == OUT_BF16X2 && ep.kind != EPI_RESID && sh.dst_plane % 4 != 0)))
     return cudaErrorInvalidValue;
   if (sh.N % 64 != 0 || sh.K % 8 != 0 || (sh.nseg != 1 && sh.nseg != 3)) return cudaErrorInvalidValue;
+  // every K slice must own at least one K block: a slice without one would store an accumulator it
+  // never wrote as its partial
+  if (sh.splits > 1 && sh.splits > ((sh.K + 63) / 64) * sh.nseg) return cudaErrorInvalidValue;
   if (ep.ln_w && (ep.kind != EPI_RESID || sh.splits < 2 || sh.N % 256 != 0 || sh.N > 1024 || !ep.ln_out ||
                   (ep.ln_planes != 1 && ep.ln_planes != 2) ||
                   ((reinterpret_cast<uintptr_t>(ep.ln_w) | reinterpret_cast<uintptr_t>(ep.ln_out)) & 15) != 0 ||

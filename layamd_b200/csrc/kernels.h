@@ -232,4 +232,11 @@ struct HeadOutArgs {
 };
 cudaError_t head_out_launch(const HeadOutArgs& a, cudaStream_t st);
 
+// ------------------------------------------------------------------ kernel-level C entry points
+// Error word shared by the kernel-level entry points on device `dev` (laya_b200_gemm,
+// laya_b200_gemm_splitk, laya_b200_attention, laya_b200_watchdog_selftest): allocated and zeroed on
+// first use, then sticky (first writer wins) until a synchronous call or laya_b200_kernel_error
+// reads and clears it. Null if the allocation failed.
+int* entry_error_word(int dev);
+
 }  // namespace laya

@@ -5,6 +5,7 @@
 // waits on a barrier phase that no thread or copy ever completes, the budget runs out, the code is
 // recorded, and the kernel returns normally.
 #include "common.cuh"
+#include "kernels.h"
 #include "laya_api.h"
 
 namespace laya {
@@ -33,12 +34,21 @@ __global__ void watchdog_selftest_kernel(int* err, long long* cycles) {
 extern "C" int laya_b200_watchdog_selftest(int device, int* code, long long* cycles, float* ms) {
   if (!code || !cycles || !ms) return -2;
   if (cudaSetDevice(device) != cudaSuccess) return -2;
-  int* d_err = nullptr;
+  // the kernel records its code in the error word of the kernel-level entry points, where it stays
+  // (first writer wins) until laya_b200_kernel_error or a synchronous entry call reads it
+  int* d_err = laya::entry_error_word(device);
   long long* d_cyc = nullptr;
   cudaEvent_t a = nullptr, b = nullptr;
   int rc = -2;
-  if (cudaMalloc(&d_err, sizeof(int)) == cudaSuccess && cudaMalloc(&d_cyc, 2 * sizeof(long long)) == cudaSuccess &&
-      cudaMemset(d_err, 0, sizeof(int)) == cudaSuccess && cudaMemset(d_cyc, 0, 2 * sizeof(long long)) == cudaSuccess &&
+  if (!d_err) return -2;
+  {
+    // a code still pending from an earlier call would hide this kernel's: report it instead
+    int pending = 0;
+    if (cudaMemcpy(&pending, d_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -2;
+    if (pending) return -3;
+  }
+  if (cudaMalloc(&d_cyc, 2 * sizeof(long long)) == cudaSuccess &&
+      cudaMemset(d_cyc, 0, 2 * sizeof(long long)) == cudaSuccess &&
       cudaEventCreate(&a) == cudaSuccess && cudaEventCreate(&b) == cudaSuccess) {
     cudaEventRecord(a, 0);
     laya::watchdog_selftest_kernel<<<1, 32>>>(d_err, d_cyc);
@@ -55,7 +65,6 @@ extern "C" int laya_b200_watchdog_selftest(int device, int* code, long long* cyc
   }
   if (a) cudaEventDestroy(a);
   if (b) cudaEventDestroy(b);
-  if (d_err) cudaFree(d_err);
   if (d_cyc) cudaFree(d_cyc);
   return rc;
 }

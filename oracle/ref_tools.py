@@ -23,8 +23,14 @@ OUT = os.path.join(ROOT, "oracle", "_ref")
 TOOLS = ("bench_engine", "test_parity")
 
 
+def reference_root():
+    """The reference checkout: LAYA_REFERENCE, else a directory named ``reference`` beside this
+    repository's root."""
+    return os.environ.get("LAYA_REFERENCE") or os.path.join(os.path.dirname(ROOT), "reference")
+
+
 def reference_src():
-    return os.path.join(os.environ.get("LAYA_REFERENCE", "/root/reference"), "src")
+    return os.path.join(reference_root(), "src")
 
 
 def wrapper_source(tool, ref_src=None):

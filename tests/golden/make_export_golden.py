@@ -22,7 +22,9 @@ sys.path.insert(0, ROOT)
 from tests import export_cases  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("LAYA_REFERENCE", "/root/reference")
+from oracle.ref_tools import reference_root  # noqa: E402
+
+REF = reference_root()
 
 
 def main():

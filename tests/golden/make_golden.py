@@ -1,8 +1,8 @@
 """Generates the golden fixtures in tests/golden/ by running the reference's own PyTorch path.
 
-Run in the build container (it imports the reference's ref/rl_common.py from LAYA_REFERENCE, default
-/root/reference, plus the installed transformers ModernBertModel; neither exists on the GPU boxes,
-which only read the committed .npz files):
+Run in the build container (it imports the reference's ref/rl_common.py from the reference checkout,
+LAYA_REFERENCE or a directory named "reference" beside the repository, plus the installed transformers
+ModernBertModel; neither exists on the GPU boxes, which only read the committed .npz files):
 
     python tests/golden/make_golden.py
 
@@ -28,7 +28,9 @@ sys.path.insert(0, ROOT)
 from layamd_b200.synthetic import synth, workloads  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("LAYA_REFERENCE", "/root/reference")
+from oracle.ref_tools import reference_root  # noqa: E402
+
+REF = reference_root()
 
 
 def fingerprint(weights):

@@ -29,7 +29,9 @@ sys.path.insert(0, ROOT)
 from layamd_b200.synthetic import synth  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("LAYA_REFERENCE", "/root/reference")
+from oracle.ref_tools import reference_root  # noqa: E402
+
+REF = reference_root()
 TOK_DIR = os.path.join(HERE, "server_tok")
 
 CFGS = [

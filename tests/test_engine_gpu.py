@@ -310,20 +310,49 @@ def test_splitk_engine_matches_whole_k(large_ckpt, large_bf16):
     assert np.array_equal(lo2, lo3) and np.array_equal(ac2, ac3)
 
 
-def test_multi_device_sharding_matches_one_device(tiny_ckpt):
-    """One handle over several GPUs (LAYA_DEVICES-style device list) shards each call's questions;
-    every question's outputs equal the single-GPU ones."""
+def _device_list():
+    """Every GPU of the box, or two replicas on GPU 0 when there is only one (each replica has its own
+    weights, arena, stream and graphs, so the sharded path runs the same way)."""
     n = torch.cuda.device_count()
-    if n < 2:
-        pytest.skip("needs 2 GPUs")
+    return ",".join(str(i) for i in range(n)) if n >= 2 else "0,0"
+
+
+def test_multi_device_sharding_matches_one_device(tiny_ckpt):
+    """One handle over several replicas (LAYA_DEVICES-style device list) shards each call's questions;
+    every question's outputs equal the single-replica ones."""
     qs = workloads.mixed(synth.ARCHS["tiny"], 50, seed=13, kmax=6)
+    devs = _device_list()
     one = Handle(tiny_ckpt, 1, devices="0", env=ENV)
-    many = Handle(tiny_ckpt, 1, devices=",".join(str(i) for i in range(min(n, 4))), env=ENV)
+    many = Handle(tiny_ckpt, 1, devices=devs, env=ENV)
     try:
-        assert many.L.laya_num_devices(many.h) == min(n, 4)
+        assert many.L.laya_num_devices(many.h) == len(devs.split(","))
+        r1 = one.forward(qs)
+        for _ in range(2):  # the replicas' workers are reused by the second call
+            r2 = many.forward(qs)
+            assert r1[0] == 0 and r2[0] == 0
+            assert rel(r2[1], r1[1]) < 1e-5 and rel(r2[2], r1[2]) < 1e-5
+    finally:
+        one.close()
+        many.close()
+
+
+def test_replica_failure_is_reported_and_the_next_call_succeeds(tiny_ckpt):
+    """Host-side failure injection (LAYA_FAIL_REPLICA=1): replica 1 returns an error for its next shard
+    before uploading or launching anything. The sharded call returns -2 only after every replica has
+    finished its part; the next call on the same handle runs every replica and matches one device."""
+    qs = workloads.mixed(synth.ARCHS["tiny"], 40, seed=21, kmax=5)
+    devs = _device_list()
+    one = Handle(tiny_ckpt, 0, devices="0", env=ENV)
+    many = Handle(tiny_ckpt, 0, devices=devs, env=dict(ENV, LAYA_FAIL_REPLICA="1:1"))
+    try:
+        rc, lo, ac = many.forward(qs)
+        assert rc == -2
+        # the replicas that did run wrote their shards: some questions have results, others not
+        assert np.isfinite(ac).any() and np.isnan(ac).any()
         r1 = one.forward(qs)
         r2 = many.forward(qs)
         assert r1[0] == 0 and r2[0] == 0
+        assert np.isfinite(r2[2]).all()
         assert rel(r2[1], r1[1]) < 1e-5 and rel(r2[2], r1[2]) < 1e-5
     finally:
         one.close()

@@ -7,8 +7,9 @@ checks call it through the C ABI twice in a row, on two different problems, and 
 with the allocating entry point laya_b200_gemm_splitk and with an fp64 reference, at the tolerances
 of the other GEMM tests (1e-4 relative for fp32 results, 1e-2 for bf16). The second call inherits the
 array from the first (partials and error word), so it also checks that nothing a call leaves there
-leaks into the next one. This file
-sorts last so that a run stopping at its first failure has already run every other test.
+leaks into the next one. A further check reads the device's free memory around a call to show that
+it allocates nothing. This file sorts last so that a run stopping at its first failure has already
+run every other test.
 """
 import ctypes
 
@@ -76,6 +77,57 @@ def test_noalloc_matches_allocating_entry_two_calls_in_a_row(lib):
     ref2 = A2.double() @ W2.double().T
     assert _rel(x_na, x_al) < 1e-4 and _rel(x_na, ref1) < 1e-4
     assert _rel(o_na, o_al) < 1e-2 and _rel(o_na, ref2) < 1e-2
+
+
+def test_noalloc_call_allocates_no_device_memory(lib):
+    """The property the entry point exists for. After a warm-up call (set-up, and the lazy loading of
+    the kernels it launches), a call on another shape leaves the device's free memory unchanged,
+    while the allocating entry point grows its workspace for a problem larger than any before it."""
+    g = torch.Generator(device="cuda").manual_seed(11)
+    shapes = [(384, 1024, 2624, 4), (256, 2048, 1024, 2)]  # splits x M x N <= 4 Mi partials
+    ins = []
+    for M, N, K, sp in shapes:
+        A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+        W = (0.02 * torch.randn(N, K, device="cuda", generator=g)).bfloat16()
+        ins.append((A, W, torch.zeros(M, N, device="cuda"), M, N, K, sp))
+    Mb, Nb, Kb, spb = 4096, 3072, 1024, 8  # 100 M partials (400 MB), beyond every other test's workspace
+    Ab = torch.randn(Mb, Kb, device="cuda", generator=g).bfloat16()
+    Wb = (0.02 * torch.randn(Nb, Kb, device="cuda", generator=g)).bfloat16()
+    ob = torch.zeros(Mb, Nb, device="cuda")
+    na = lib.laya_b200_gemm_splitk_noalloc
+    A, W, o, M, N, K, sp = ins[0]
+    assert _call(na, A, W, o, M, N, K, sp) == 0  # warm-up
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    A, W, o, M, N, K, sp = ins[1]
+    assert _call(na, A, W, o, M, N, K, sp) == 0
+    torch.cuda.synchronize()
+    free1 = torch.cuda.mem_get_info()[0]
+    assert free1 == free0, "the allocation-free entry changed free device memory by %d bytes" % (free0 - free1)
+    assert _rel(o, A.double() @ W.double().T) < 1e-4
+    assert _call(lib.laya_b200_gemm_splitk, Ab, Wb, ob, Mb, Nb, Kb, spb) == 0
+    torch.cuda.synchronize()
+    free2 = torch.cuda.mem_get_info()[0]
+    assert free1 - free2 >= spb * Mb * Nb * 4  # the allocating entry did grow its workspace
+
+
+def test_split_count_beyond_the_k_blocks_is_rejected(lib):
+    """Every K slice must own a K block, or its partial plane would hold an accumulator nobody wrote:
+    K = 128 has two 64-wide blocks, so 4 slices are refused by both split-K entries before anything
+    is launched, and 2 slices give the right product."""
+    g = torch.Generator(device="cuda").manual_seed(12)
+    M, N, K = 256, 512, 128
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    W = (0.02 * torch.randn(N, K, device="cuda", generator=g)).bfloat16()
+    for fn in (lib.laya_b200_gemm_splitk_noalloc, lib.laya_b200_gemm_splitk):
+        out = torch.full((M, N), 3.0, device="cuda")
+        assert _call(fn, A, W, out, M, N, K, 4) == -2
+        torch.cuda.synchronize()
+        assert bool((out == 3.0).all())
+        assert _call(fn, A, W, out, M, N, K, 2) == 0
+        torch.cuda.synchronize()
+        assert _rel(out, A.double() @ W.double().T) < 1e-4
+    assert lib.laya_b200_kernel_error(0) == 0  # and no kernel recorded an error
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch(lib):
