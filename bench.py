@@ -14,6 +14,10 @@ Per step (one forward pass over the 192 questions):
   roofline  the encoder GEMM family: algorithmic 2*M*N*K FLOPs of one pass over their device time,
          from CUDA events around every stage inside the replayed pass graph (laya_replay_profiled),
          against the measured sustained bf16 peak of MEASURED_PEAKS.json.
+  hbm_roofline  the bandwidth-bound stages (attention, LayerNorm, embedding) the same way: algorithmic
+         bytes over in-graph device time against the measured HBM copy bandwidth.
+  seq512 the fixed-length shape of the metric's name: 128 questions x 512 tokens x 3 options per
+         rank, resident in HBM and replayed like value (a named extra; value stays C2).
 Multi-GPU (torchrun, one rank per GPU): every rank serves its own 192 questions on its own GPU;
 questions are independent, so there is no collective on the data path (weak scaling). Ranks only
 meet at barriers and for the max-over-ranks timing reduction (gloo).
@@ -175,6 +179,45 @@ def load_peaks():
         return 1400.0, "fallback (1.4 PFLOP/s sustained)"
 
 
+def load_hbm_peak():
+    try:
+        with open(PEAKS) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return 6650.0, "fallback (6.65 TB/s)"
+
+
+def hbm_rooflines(qs, arch, prof):
+    """HBM fraction of the bandwidth-bound encoder stages from their in-graph device times.
+
+    Algorithmic bytes over the valid rows T of one pass (hidden size D, bf16 activations, fp32
+    residual stream):
+      attention (per launch)   read q, k, v once (6D) + write the output (2D)  = 8D per row
+      LayerNorm (ln stage)     read x fp32 (4D) + write xn bf16 (2D) = 6D per row; the last one of
+                               the encoder also writes x back (final norm + type embedding), +4D
+      embedding + LayerNorm    read the fp32 embedding row (4D) + write x (4D) + xn (2D) = 10D
+    """
+    T = sum(len(q["ids"]) for q in qs)
+    D = arch.d
+    peak, src = load_hbm_peak()
+    out = {"peak_gbs": peak, "peak_source": src, "rows": T}
+    spec = {
+        "attn_global": lambda n: n * 8 * D * T,
+        "attn_sliding": lambda n: n * 8 * D * T,
+        "ln": lambda n: n * 6 * D * T + (4 * D * T if n else 0),
+        "embed_ln": lambda n: n * 10 * D * T,
+    }
+    for name, fn in spec.items():
+        if name not in prof or prof[name][0] <= 0:
+            continue
+        ms, n = prof[name]
+        byt = fn(n)
+        gbs = byt / (ms / 1e3) / 1e9
+        out[name] = {"launches": int(n), "ms": round(ms, 4), "bytes_per_launch": int(byt // max(n, 1)),
+                     "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 3)}
+    return out
+
+
 STAGES = ["gemm_qkv", "gemm_attn_out", "gemm_mlp_in", "gemm_mlp_out", "attn_global", "attn_sliding", "ln",
           "embed_ln", "head_gemm", "head_attn", "head_ln", "scorer", "head_out"]
 
@@ -268,6 +311,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--latency-calls", type=int, default=100)
+    ap.add_argument("--seq512-steps", type=int, default=10)
     args = ap.parse_args()
     rank, local, world = dist_env()
     if args.impl == "reference":
@@ -344,6 +388,26 @@ def main():
         except Exception:
             traffic = None
 
+    # ---- fixed length 512 (the metric's seq512): 128 questions x 512 tokens x 3 options, resident in
+    # HBM and replayed like `value`
+    seq = None
+    if args.seq512_steps > 0:
+        qs5 = workloads.seq512(arch, seed=5 + rank)
+        l5, i5, n5, m5, t5 = abi_arrays(qs5)
+        assert L.laya_stage(h, len(qs5), p(l5), p(i5), p(n5), p(m5), p(t5)) == 0
+        ms5 = ctypes.c_double(0)
+        assert L.laya_replay(h, 3, ctypes.byref(ms5)) == 0
+        dist.barrier()
+        assert L.laya_replay(h, args.seq512_steps, ctypes.byref(ms5)) == 0
+        dist.barrier()
+        ms5v = dist.max(ms5.value)
+        f5 = decision_flops(qs5, arch)
+        seq = {"decisions_per_s": len(qs5) * world * args.seq512_steps / (ms5v / 1e3),
+               "ms_per_step": ms5v / args.seq512_steps, "steps": args.seq512_steps,
+               "questions_per_rank": len(qs5), "tokens_per_rank": int(l5.sum()),
+               "model_tflops": f5 * world / (ms5v / args.seq512_steps / 1e3) / 1e12,
+               "shape": "128 choice questions x 512 tokens x 3 options per rank, one packed pass, inputs in HBM"}
+
     # ---- batch-1 latency at the C1 shape (L=512, one 3-option question)
     lat = None
     if rank == 0 and args.latency_calls > 0:
@@ -388,6 +452,8 @@ def main():
                                    % (g_launch, g_ms), "peak_source": peak_src},
             "model_flops_per_step": decision_flops(qs, arch),
             "model_tflops": decision_flops(qs, arch) * world / (dev_ms / args.steps / 1e3) / 1e12,
+            "hbm_roofline": hbm_rooflines(qs, arch, prof),
+            "seq512": seq,
             "stages_ms": {k: round(v[0], 4) for k, v in prof.items()},
             "stages_note": "device time per pass of each stage, CUDA events around every stage inside the replayed "
                            "pass graph (laya_replay_profiled), last of 5 back-to-back replays after the timed region",

@@ -49,6 +49,12 @@ def c2(arch, states=64, seed=1):
     return qs
 
 
+def seq512(arch, B=128, L=512, seed=5):
+    """Fixed length: B choice questions of exactly L tokens with 3 options each (the metric's seq512)."""
+    rng = np.random.default_rng(seed)
+    return [_question(rng, L, 3, 0, arch) for _ in range(B)]
+
+
 def c3(arch, B=128, seed=3):
     """mmBERT-base shapes: L ~ U[64,1024], ids over the whole vocabulary, one 3-option choice each."""
     rng = np.random.default_rng(seed)

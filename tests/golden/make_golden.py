@@ -4,7 +4,9 @@ Run in the build container (it imports the reference's ref/rl_common.py from the
 LAYA_REFERENCE or a directory named "reference" beside the repository, plus the installed transformers
 ModernBertModel; neither exists on the GPU boxes, which only read the committed .npz files):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py              # every fixture
+    python tests/golden/make_golden.py --configs    # only the C3 / C4 ones
+    python tests/golden/make_golden.py --c2         # only the C2 batch's logits
 
 What it does, following ref/gen_golden.py:51-105 of the reference:
   1. builds each synthetic checkpoint with layamd_b200.synthetic.synth (seeded init rule) and checks that the
@@ -149,7 +151,71 @@ def main():
     lo, ac, acts, b = run_reference(model, rl, a, qs)
     save_case(os.path.join(HERE, "large_multi.npz"), qs, lo, ac, acts, full=False, sample_rows=[0, 1, 2])
     print("[golden] large_multi lens=%s" % [len(q["ids"]) for q in qs], flush=True)
+    del model
+    configs()
+    c2_batch()
+
+
+def configs():
+    """The other benchmark configurations: mmBERT-base (C3: vocabulary 256,000, pad id 0, 22 layers,
+    d 768) and ModernBERT-large at context 1024 (C4: RoPE positions 512-1023, global attention over
+    more than 512 keys), each with a question longer than 900 tokens in a padded batch."""
+    # C3: token ids over the whole vocabulary (pad id 0 included inside a sequence, as C3 draws them)
+    a = synth.ARCHS["base"]
+    ck = synth.checkpoint("base", 0)
+    model, rl, w = reference_model(ck)
+    np.savez_compressed(os.path.join(HERE, "base_weights_fp.npz"), **fingerprint(w))
+    rng = np.random.default_rng(31)
+    qs = [workloads._question(rng, 987, 3, 0, a, id_lo=0), workloads._question(rng, 301, 3, 0, a, id_lo=0)]
+    lo, ac, acts, b = run_reference(model, rl, a, qs)
+    save_case(os.path.join(HERE, "base_c3.npz"), qs, lo, ac, acts, full=False,
+              sample_rows=[0, 1, 2, 511, 512, 700, 900, 986])
+    print("[golden] base_c3 lens=%s" % [len(q["ids"]) for q in qs], flush=True)
+    del model
+    # C4: the ModernBERT-large weights with a context-1024 agent config; all three question types
+    a = synth.ARCHS["large1024"]
+    ck = synth.checkpoint("large1024", 0)
+    model, rl, w = reference_model(ck)
+    np.savez_compressed(os.path.join(HERE, "large1024_weights_fp.npz"), **fingerprint(w))
+    rng = np.random.default_rng(41)
+    qs = [workloads._question(rng, 1021, 4, 1, a), workloads._question(rng, 377, 2, 2, a),
+          workloads._question(rng, 733, 6, 0, a)]
+    lo, ac, acts, b = run_reference(model, rl, a, qs)
+    save_case(os.path.join(HERE, "large1024_c4.npz"), qs, lo, ac, acts, full=False,
+              sample_rows=[0, 1, 17, 511, 512, 513, 800, 1020])
+    print("[golden] large1024_c4 lens=%s" % [len(q["ids"]) for q in qs], flush=True)
+
+
+def c2_batch():
+    """Logits and act logits of the reference for the whole C2 benchmark batch (ModernBERT-large, 64
+    states x 3 questions, seed 1), run in length-sorted padded batches of 16 as predict_items does
+    (ref/rl_common.py:370-408); no hooks."""
+    import torch
+    a = synth.ARCHS["large"]
+    ck = synth.checkpoint("large", 0)
+    model, rl, w = reference_model(ck)
+    qs = workloads.c2(a, seed=1)
+    order = sorted(range(len(qs)), key=lambda i: len(qs[i]["ids"]))
+    logits = [None] * len(qs)
+    act = np.zeros((len(qs), a.n_act), np.float32)
+    for s in range(0, len(order), 16):
+        idx = order[s:s + 16]
+        lo, ac, _, _ = run_reference(model, rl, a, [qs[i] for i in idx])
+        for r, i in enumerate(idx):
+            logits[i] = lo[r, :len(qs[i]["markers"])]
+            act[i] = ac[r]
+    lens, ids, nmark, markers, qtypes = workloads.flatten(qs)
+    np.savez_compressed(os.path.join(HERE, "large_c2_logits.npz"), lens=lens, nmark=nmark, qtypes=qtypes,
+                        markers=markers, ids_sum=np.int64(ids.astype(np.int64).sum()),
+                        logits=np.concatenate(logits).astype(np.float32), act=act)
+    print("[golden] large_c2_logits: %d questions, %d tokens" % (len(qs), int(lens.sum())), flush=True)
 
 
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] in (["--configs"], ["--c2"]):
+        import torch
+        torch.set_grad_enabled(False)
+        torch.set_num_threads(os.cpu_count() or 8)
+        configs() if sys.argv[1] == "--configs" else c2_batch()
+    else:
+        main()

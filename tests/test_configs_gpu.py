@@ -2,6 +2,8 @@
 checkpoints: mmBERT-base (C3: d 768, 12 heads, 22 layers, GeGLU 1152, vocabulary 256000, pad id 0,
 context 1024) and ModernBERT-large at context 1024 (C4: sequences past 512 tokens, RoPE positions
 and global attention up to 1024 keys), in fp32-parity and bf16 mode."""
+import os
+
 import numpy as np
 import pytest
 
@@ -13,6 +15,7 @@ from tests.engine_helpers import Handle, act_rel, argmax_agree, gathered_rows, p
 
 pytestmark = pytest.mark.gpu
 ENV = {"LAYA_MAX_TOKENS": 16384}
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -72,3 +75,40 @@ def test_large_context_1024_c4_shapes():
     bad = {k: v for k, v in worst.items() if v > 1e-3}
     assert not bad, bad
     assert np.isfinite(lo).all()
+
+
+@pytest.mark.parametrize("arch,case", [("base", "base_c3"), ("large1024", "large1024_c4")])
+def test_fp32_parity_against_reference_golden(arch, case):
+    """The engine in fp32-parity mode against the reference's own outputs at C3 and C4
+    (tests/golden/base_c3.npz, large1024_c4.npz: ref/rl_common.py + transformers on the same seeded
+    checkpoint): probabilities within 1e-4, act logits within 1e-3, and per layer the row norms of
+    every packed row and the full sampled rows of the first (longest) question within
+    max|a-b|/max|b| <= 1e-3."""
+    ck = synth.checkpoint(arch, 0)
+    a = synth.load_arch(ck)
+    g = np.load(os.path.join(GOLD, case + ".npz"))
+    qs, io, mo = [], 0, 0
+    for L, k, qt in zip(g["lens"], g["nmark"], g["qtypes"]):
+        qs.append({"ids": g["ids"][io:io + L].tolist(), "markers": g["markers"][mo:mo + k].tolist(), "qtype": int(qt)})
+        io += L
+        mo += k
+    h = Handle(ck, 1, env=ENV)
+    try:
+        lo, ac, d = h.forward_dump(qs)
+    finally:
+        h.close()
+    assert prob_delta(lo, g["logits"], qs) <= 1e-4
+    assert act_rel(ac, g["act"]) <= 1e-3
+    lens = [len(q["ids"]) for q in qs]
+    T = sum(lens)
+    rows = g["sample_rows"]
+    worst = {}
+    for key in ["emb"] + ["enc%d" % i for i in range(a.layers)] + ["head0"]:
+        t = read_dump(d, key, a.d)[:T]
+        worst[key] = max(rel(np.linalg.norm(t, axis=-1), g["n_" + key]), rel(t[rows], g["s_" + key]))
+    offs = np.cumsum([0] + lens[:-1])
+    idx = [int(o + m) for o, q in zip(offs, qs) for m in q["markers"]] + [int(o) for o in offs]
+    t = read_dump(d, "head1", a.d)[:len(idx)]  # gathered rows: every question's markers, then its CLS row
+    worst["head1"] = rel(np.linalg.norm(t, axis=-1), g["n_head1"][idx])
+    bad = {k: v for k, v in worst.items() if v > 1e-3}
+    assert not bad, bad

@@ -161,22 +161,21 @@ def test_large_c1_bf16(large_bf16, large_oracle):
     assert act_rel(ac, ac_o) < 0.05
 
 
-def test_large_c2_bf16_subset_vs_oracle(large_bf16, large_oracle):
+def test_large_c2_bf16_all_192_vs_reference(large_bf16):
+    """The benchmark's own batch, every question: C2 (64 states x 3 questions, 52,287 tokens) through
+    one laya_forward_batch call in bf16, against the reference PyTorch path's fp32 logits for the same
+    192 questions (tests/golden/large_c2_logits.npz, made by make_golden.py --c2)."""
     qs = workloads.c2(synth.ARCHS["large"])
+    g = np.load(os.path.join(GOLD, "large_c2_logits.npz"))
+    lens, ids, nmark, markers, qtypes = workloads.flatten(qs)
+    assert (lens == g["lens"]).all() and (nmark == g["nmark"]).all() and (markers == g["markers"]).all()
+    assert int(ids.astype(np.int64).sum()) == int(g["ids_sum"])
     rc, lo, ac = large_bf16.forward(qs)
     assert rc == 0 and np.isfinite(lo).all() and np.isfinite(ac).all()
-    sub = list(range(0, len(qs), 16))  # 12 questions of every type and length range
-    qsub = [qs[i] for i in sub]
-    lo_o, ac_o, _ = large_oracle.forward_batch(qsub)
-    per = []
-    o = 0
-    for q in qs:
-        per.append(lo[o:o + len(q["markers"])])
-        o += len(q["markers"])
-    lo_s = np.concatenate([per[i] for i in sub])
-    assert prob_delta(lo_s, lo_o, qsub) < 0.01
-    assert act_rel(ac[sub], ac_o) < 0.05
-    assert argmax_agree(lo_s, lo_o, qsub)
+    assert len(qs) == 192
+    assert prob_delta(lo, g["logits"], qs) < 0.01
+    assert act_rel(ac, g["act"]) < 0.05
+    assert argmax_agree(lo, g["logits"], qs)
 
 
 def test_validation_contract(tiny_bf16):

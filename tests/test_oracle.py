@@ -76,9 +76,63 @@ def test_large(case):
         assert rel(caps[0][key][rows], g["s_" + key]) < 5e-5, key
 
 
+@pytest.mark.slow
+@pytest.mark.parametrize("arch,case,layers", [("base", "base_c3", 22), ("large1024", "large1024_c4", 28)])
+def test_other_configurations(arch, case, layers):
+    """C3 (mmBERT-base: vocabulary 256,000, pad id 0, 22 layers, d 768; a 987-token question) and C4
+    (ModernBERT-large at context 1024: RoPE positions up to 1020, global attention over 1021 keys),
+    each in a padded batch with shorter questions, against the reference's own path."""
+    ck = synth.checkpoint(arch, 0)
+    w = synth.load_weights(ck)
+    check_fingerprint(w, arch + "_weights_fp.npz")
+    o = om.Oracle(w, synth.load_arch(ck))
+    g = np.load(os.path.join(GOLD, case + ".npz"))
+    qs = questions_of(g)
+    assert max(len(q["ids"]) for q in qs) > 900
+    lo, ac, caps = o.forward_batch(qs, capture=True)
+    assert np.abs(lo - g["logits"]).max() < 2e-5
+    assert np.abs(ac - g["act"]).max() < 2e-5 * max(1.0, np.abs(g["act"]).max())
+    rows = g["sample_rows"]
+    for key in ["emb", "final_norm", "head0", "head1"] + ["enc%d" % i for i in range(layers)]:
+        norms = np.concatenate([np.linalg.norm(c[key], axis=-1) for c in caps])
+        assert rel(norms, g["n_" + key]) < 2e-5, key
+        assert rel(caps[0][key][rows], g["s_" + key]) < 5e-5, key
+
+
 def test_rope_tables_match_transformers_formula():
     cos, sin = om.rope_tables(8, 10000.0)
     inv = 1.0 / (10000.0 ** (np.arange(0, 64, 2) / 64))
     f = np.arange(8)[:, None] * inv[None, :]
     assert np.abs(cos[:, :32] - np.cos(f)).max() < 1e-6
     assert np.abs(sin[:, 32:] - np.sin(f)).max() < 1e-6
+
+
+def test_c2_golden_inputs_are_the_benchmark_batch():
+    """The reference logits of the whole C2 batch were made on exactly the inputs the benchmark and
+    the GPU test generate (lengths, option counts, marker positions, token-id checksum)."""
+    from layamd_b200.synthetic import workloads
+    g = np.load(os.path.join(GOLD, "large_c2_logits.npz"))
+    lens, ids, nmark, markers, qtypes = workloads.flatten(workloads.c2(synth.ARCHS["large"], seed=1))
+    assert (lens == g["lens"]).all() and (nmark == g["nmark"]).all() and (qtypes == g["qtypes"]).all()
+    assert (markers == g["markers"]).all() and int(ids.astype(np.int64).sum()) == int(g["ids_sum"])
+    assert g["logits"].shape == (int(nmark.sum()),) and g["act"].shape == (192, 2)
+    assert np.isfinite(g["logits"]).all()
+
+
+@pytest.mark.slow
+def test_oracle_on_c2_questions_matches_reference_batch():
+    """Three C2 questions (shortest, median, longest) through the oracle against the reference's
+    batched C2 logits: padding inside the reference's length-sorted batches does not change them."""
+    from layamd_b200.synthetic import workloads
+    ck = synth.checkpoint("large", 0)
+    w = synth.load_weights(ck)
+    check_fingerprint(w, "large_weights_fp.npz")
+    o = om.Oracle(w, synth.load_arch(ck))
+    qs = workloads.c2(synth.ARCHS["large"], seed=1)
+    g = np.load(os.path.join(GOLD, "large_c2_logits.npz"))
+    offs = np.concatenate([[0], np.cumsum(g["nmark"])])
+    order = sorted(range(len(qs)), key=lambda i: len(qs[i]["ids"]))
+    for i in (order[0], order[len(order) // 2], order[-1]):
+        lo, ac = o.forward_one(qs[i]["ids"], qs[i]["markers"], qs[i]["qtype"])
+        assert np.abs(lo - g["logits"][offs[i]:offs[i + 1]]).max() < 2e-5
+        assert np.abs(ac - g["act"][i]).max() < 2e-5 * max(1.0, np.abs(g["act"][i]).max())
