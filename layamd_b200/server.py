@@ -16,15 +16,17 @@ round's latency near one C2-size pass), so concurrent requests share passes on e
 question headers are tokenised in one batched call; and the worker can be stopped
 (``Batcher.close``).
 """
+import collections
 import functools
 import itertools
 import json
 import math
 import os
-import queue
 import threading
 import time
-from typing import Dict, List, Optional, Sequence, Tuple
+from concurrent.futures import Future
+from dataclasses import dataclass, field
+from typing import Deque, Dict, List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -259,84 +261,97 @@ class Laya:
         return self.finish(qids, qs, items, logits, act, t0)
 
 
+@dataclass
+class _Ticket:
+    """One request's questions waiting for a round, and the future its caller blocks on."""
+    seqs: List[List[int]]
+    markers: List[List[int]]
+    qtypes: List[int]
+    tokens: int
+    result: Future = field(default_factory=Future)
+
+
 class Batcher:
-    """Continuous batching across concurrent requests (laya_server.py:191-242).
+    """Continuous batching of concurrent requests into engine rounds.
 
-    Request threads enqueue their tokenised questions and block; one worker thread takes everything
-    queued, up to ``max_tokens`` tokens (a request is never split; one larger than the budget runs
-    alone), and makes one engine call for the round, which the engine packs back to back and shards
-    over its GPUs. A request that arrives while a round runs joins the next one; one that does not
-    fit the current round is carried over to lead the next. An engine error fails every request of
-    its round with that exception.
+    Requests are queued as tickets; a single serving thread takes the oldest pending tickets, as many
+    as fit ``max_tokens`` tokens (never splitting a request; one larger than the budget runs alone),
+    and makes ONE ``forward_batch`` call for them: the engine packs the round back to back and, on a
+    multi-GPU handle, shards it over its replicas. Tickets that arrive while a round runs, or that did
+    not fit it, stay queued in arrival order for the next round. Each caller waits on its ticket's
+    future; if the engine call raises, every ticket of that round receives the exception and the
+    thread goes on serving. The observable rules (a token budget per round, arrival order, one call
+    per round, an error fails its whole round) are the reference server's worker
+    (server/laya_server.py:191-242); the structure here is its own.
 
-    ``max_tokens`` defaults to 65536 tokens per GPU of the engine (``num_devices``), so that one
+    ``max_tokens`` defaults to DEFAULT_PASS_TOKENS per GPU of the engine (``num_devices``), so one
     round fills every GPU's pass."""
 
     def __init__(self, engine, max_tokens: Optional[int] = None):
         if max_tokens is None:
             max_tokens = DEFAULT_PASS_TOKENS * max(1, int(getattr(engine, "num_devices", 1) or 1))
         self.engine, self.max_tokens = engine, int(max_tokens)
-        self.q: "queue.Queue" = queue.Queue()
-        self.carry = None
         self.stats = {"passes": 0, "questions": 0, "tokens": 0}
-        self._stop = object()
-        self._thread = threading.Thread(target=self._loop, daemon=True, name="laya-batcher")
-        self._thread.start()
+        self._pending: Deque[_Ticket] = collections.deque()
+        self._cv = threading.Condition()
+        self._closing = False
+        self._server = threading.Thread(target=self._serve, daemon=True, name="laya-batcher")
+        self._server.start()
+
+    def submit(self, items) -> Future:
+        """Queues one request's questions (``(token ids, markers, qtype)`` each); the future resolves to
+        (per-question logits, act rows) once its round has run."""
+        t = _Ticket([it[0] for it in items], [it[1] for it in items], [it[2] for it in items],
+                    sum(len(it[0]) for it in items))
+        with self._cv:
+            if self._closing:
+                raise RuntimeError("batcher is closed")
+            self._pending.append(t)
+            self._cv.notify()
+        return t.result
 
     def run(self, items):
         """Blocks until the round holding ``items`` has run; returns (per-question logits, act rows)."""
-        job = {"items": items, "ev": threading.Event(), "logits": [None] * len(items), "act": [None] * len(items),
-               "err": None, "tokens": sum(len(it[0]) for it in items)}
-        self.q.put(job)
-        job["ev"].wait()
-        if job["err"] is not None:
-            raise job["err"]
-        return job["logits"], job["act"]
+        return self.submit(items).result()
 
     def close(self, timeout: float = 10.0):
-        """Stops the worker after the rounds already queued."""
-        self.q.put(self._stop)
-        self._thread.join(timeout)
+        """Refuses new requests, serves the ones already queued, then stops the serving thread."""
+        with self._cv:
+            self._closing = True
+            self._cv.notify()
+        self._server.join(timeout)
 
-    def _round(self):
-        first = self.carry if self.carry is not None else self.q.get()
-        self.carry = None
-        if first is self._stop:
-            return None
-        jobs, tokens = [first], first["tokens"]
-        while True:
-            try:
-                j = self.q.get_nowait()
-            except queue.Empty:
-                break
-            if j is self._stop:
-                self.q.put(j)  # finish this round, then stop
-                break
-            if tokens + j["tokens"] > self.max_tokens:
-                self.carry = j
-                break
-            jobs.append(j)
-            tokens += j["tokens"]
-        return jobs, tokens
+    def _take_round(self) -> Optional[List[_Ticket]]:
+        with self._cv:
+            self._cv.wait_for(lambda: self._pending or self._closing)
+            if not self._pending:
+                return None  # closed and drained
+            taken = [self._pending.popleft()]
+            budget = self.max_tokens - taken[0].tokens
+            while self._pending and self._pending[0].tokens <= budget:
+                budget -= self._pending[0].tokens
+                taken.append(self._pending.popleft())
+            return taken
 
-    def _loop(self):
+    def _serve(self):
         while True:
-            r = self._round()
-            if r is None:
+            tickets = self._take_round()
+            if tickets is None:
                 return
-            jobs, tokens = r
-            flat = [(ji, ii, it) for ji, j in enumerate(jobs) for ii, it in enumerate(j["items"])]
+            seqs = list(itertools.chain.from_iterable(t.seqs for t in tickets))
+            marks = list(itertools.chain.from_iterable(t.markers for t in tickets))
+            qts = list(itertools.chain.from_iterable(t.qtypes for t in tickets))
             try:
-                lg, ac = self.engine.forward_batch([f[2][0] for f in flat], [f[2][1] for f in flat],
-                                                   [f[2][2] for f in flat])
-                for (ji, ii, _), l_, a_ in zip(flat, lg, ac):
-                    jobs[ji]["logits"][ii] = l_
-                    jobs[ji]["act"][ii] = a_
-                self.stats["passes"] += 1
-                self.stats["questions"] += len(flat)
-                self.stats["tokens"] += tokens
-            except Exception as e:  # every request of the round sees the engine's error
-                for j in jobs:
-                    j["err"] = e
-            for j in jobs:
-                j["ev"].set()
+                logits, act = self.engine.forward_batch(seqs, marks, qts)
+            except Exception as e:  # the whole round fails with the engine's error
+                for t in tickets:
+                    t.result.set_exception(e)
+                continue
+            self.stats["passes"] += 1
+            self.stats["questions"] += len(seqs)
+            self.stats["tokens"] += sum(t.tokens for t in tickets)
+            lo = 0
+            for t in tickets:
+                hi = lo + len(t.seqs)
+                t.result.set_result((list(logits[lo:hi]), list(act[lo:hi])))
+                lo = hi
