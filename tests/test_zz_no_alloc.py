@@ -108,7 +108,9 @@ def test_noalloc_call_allocates_no_device_memory(lib):
     assert _call(lib.laya_b200_gemm_splitk, Ab, Wb, ob, Mb, Nb, Kb, spb) == 0
     torch.cuda.synchronize()
     free2 = torch.cuda.mem_get_info()[0]
-    assert free1 - free2 >= spb * Mb * Nb * 4  # the allocating entry did grow its workspace
+    # the allocating entry did grow its workspace: it frees its previous, smaller one (a few tens of
+    # MB from the earlier tests at most) and allocates 400 MB
+    assert free1 - free2 >= 0.75 * spb * Mb * Nb * 4
 
 
 def test_split_count_beyond_the_k_blocks_is_rejected(lib):
