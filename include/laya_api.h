@@ -24,8 +24,11 @@ void* laya_create(const char* dir);
 /* B questions in one call. ids/markers are concatenated per question; markers are positions within
  * that question's sequence. logits receive sum(nmark) raw scorer logits in input order, act B*n_act
  * raw act-head logits. Returns 0, or -1 without touching the outputs when any 1<=lens[b]<=max_len,
- * 1<=nmark[b]<=255 or 0<=marker<lens[b] fails. Replaces src/laya_api.h:8-9
- * (src/engine.hip:489-539). Also returns -2 when the GPU reported an error for this call. */
+ * 1<=nmark[b]<=255 or 0<=marker<lens[b] fails, or (an addition: the reference reads outside its
+ * embedding table instead) a token id lies outside [0, vocab) or a qtype outside 0..2. Replaces
+ * src/laya_api.h:8-9
+ * (src/engine.hip:489-539). Also returns -2 when the GPU reported an error for this call, and -3 in
+ * debug bounds mode when a pass's packing maps failed their host check (nothing was launched). */
 int laya_forward_batch(void* h, int B, const int* lens, const int* ids, const int* nmark, const int* markers,
                        const int* qtypes, float* logits, float* act);
 
@@ -93,6 +96,25 @@ int laya_plan_passes_cfg(int max_len, int pass_tokens, int max_seqs, int B, cons
  * the engine's own choice). Returns 0 or -1. */
 int laya_plan_gemm(int M, int N, int K, int parity, int num_sms, int pair_clusters, int ln_fusable, int* bn,
                    int* splits);
+
+/* No counterpart in the reference. Debug bounds mode, host side and host-only: validates a batch like
+ * laya_forward_batch (plus qtypes in 0..2 and ids inside the vocabulary), packs it into passes of at
+ * most pass_tokens rows and max_seqs questions, fills every pass's metadata block exactly as the
+ * engine uploads it (token ids, positions, row -> question map, offsets, the attention work items
+ * and gathered-row maps) and checks every map against the pass and the arena. corrupt > 0 breaks map
+ * number `corrupt` (1-8) of the first pass before the check, so a test can show that the check
+ * catches it. Returns the number of passes checked, -1 for an invalid batch, or -100-n when check n
+ * failed. The engine runs the same check on every pass when loaded with LAYA_DEBUG_BOUNDS=1 or from a
+ * debug-bounds build, and then returns -3 from laya_forward_batch without launching anything. */
+int laya_pack_check(int max_len, int vocab, int pad_id, int pass_tokens, int max_seqs, int B, const int* lens,
+                    const int* ids, const int* nmark, const int* markers, const int* qtypes, int corrupt);
+
+/* No counterpart in the reference. 1 when this library was built with -DLAYA_DEBUG_BOUNDS: every
+ * kernel then checks the indices it reads from the packing maps (token ids, rows, work items,
+ * gathered rows, marker offsets, RoPE positions) against their extents, records code 40-45 in the
+ * error word and skips the access instead of reading or writing out of range (laya_forward_batch
+ * then returns -2). 0 in the normal build, whose kernels carry no such checks. */
+int laya_debug_bounds_build(void);
 
 /* The replica (0..ndev-1) each of B questions goes to when a call is sharded over ndev GPUs, as
  * laya_forward_batch does it, for a model of hidden size d, GeGLU width `intermediate`, n_layers

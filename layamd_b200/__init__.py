@@ -67,6 +67,8 @@ def load_lib(path: str = LIB_PATH) -> ctypes.CDLL:
         "laya_b200_attention": (i, [vp, vp, i, i, _IP, i, i, i, vp, i]),
         "laya_b200_gemm_splitk_noalloc": (i, [vp, vp, vp, vp, vp, i, i, i, i, i, i, i, i, vp, vp, vp, i, i, i, vp, i]),
         "laya_b200_kernel_error": (i, [i]),
+        "laya_pack_check": (i, [i, i, i, i, i, i, _IP, _IP, _IP, _IP, _IP, i]),
+        "laya_debug_bounds_build": (i, []),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -1,5 +1,6 @@
 // C ABI of the engine (declared in include/laya_api.h). The first ten functions keep the reference's
 // names, signatures and return contract (src/engine.hip:543-559).
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -107,6 +108,45 @@ int laya_plan_passes(void* h, int B, const int* lens, const int* nmark, const in
   }
   return (int)plans.size();
 }
+
+int laya_pack_check(int max_len, int vocab, int pad_id, int pass_tokens, int max_seqs, int B, const int* lens,
+                    const int* ids, const int* nmark, const int* markers, const int* qtypes, int corrupt) {
+  if (B < 0 || (B > 0 && (!lens || !ids || !nmark || !markers || !qtypes)) || vocab <= 0 || max_len <= 0 ||
+      pad_id < 0 || pad_id >= vocab)
+    return -1;
+  if (!laya::validate_batch(B, lens, nmark, markers, max_len)) return -1;
+  for (int b = 0; b < B; ++b)
+    if (qtypes[b] < 0 || qtypes[b] > 2) return -1;
+  size_t nt = 0;
+  for (int b = 0; b < B; ++b) nt += lens[b];
+  for (size_t t = 0; t < nt; ++t)
+    if (ids[t] < 0 || ids[t] >= vocab) return -1;
+  const int rows = std::max(pass_tokens, max_len);
+  const int seqs = std::max(max_seqs, 1);
+  const int gathered = std::max(rows / 4, 2 * (laya::kMaxMarkers + 1));
+  std::vector<laya::PassPlan> plans;
+  if (!laya::plan_passes(B, lens, nmark, rows, seqs, gathered, &plans)) return -1;
+  std::vector<laya::Question> qs(B);
+  size_t io = 0, mo = 0;
+  for (int b = 0; b < B; ++b) {
+    qs[b] = laya::Question{lens[b], nmark[b], qtypes[b], ids + io, markers + mo, nullptr, nullptr};
+    io += lens[b];
+    mo += nmark[b];
+  }
+  const laya::PackLimits lim{vocab, max_len, (rows + 63) / 64 * 64, gathered, seqs};
+  std::vector<int> meta;
+  for (size_t i = 0; i < plans.size(); ++i) {
+    const laya::PassPlan& p = plans[i];
+    meta.assign(laya::pass_meta_ints(p), 0);
+    laya::fill_pass_meta(p, qs.data(), pad_id, meta.data());
+    if (i == 0 && corrupt > 0) laya::corrupt_pass_meta(p, meta.data(), corrupt, vocab);
+    const int bad = laya::check_pass_meta(p, meta.data(), lim);
+    if (bad) return -100 - bad;
+  }
+  return static_cast<int>(plans.size());
+}
+
+int laya_debug_bounds_build(void) { return laya::kDebugBoundsBuild ? 1 : 0; }
 
 int laya_shard_plan(int ndev, int B, const int* lens, const int* nmark, int d, int intermediate, int n_layers,
                     int n_global, int window, int* owner) {

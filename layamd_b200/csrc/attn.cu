@@ -63,10 +63,15 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const AttnArgs a) {
   pdl_wait();
   const AttnItem it = a.items[blockIdx.x];
   if (it.seq < 0) return;
+  if (!LAYA_IN_BOUNDS(a.n_seq <= 0 || it.seq < a.n_seq, a.err, kErrBoundsAttn)) return;
   const int h = blockIdx.y;
   const int D = a.H * 64;
   const long long ld = 3LL * D;
   const int base = a.soff[it.seq], len = a.slen[it.seq];
+  if (!LAYA_IN_BOUNDS(a.rows <= 0 || (base >= 0 && len > 0 && base + len <= a.rows &&
+                                      (GATHER ? (it.nq >= 1 && it.nq <= 64) : (it.q0 >= 0 && it.q0 < len))),
+                      a.err, kErrBoundsAttn))
+    return;
   const bf16* qkv = static_cast<const bf16*>(a.qkv);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
@@ -76,6 +81,12 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const AttnArgs a) {
     if (tid < 64) {
       s_src[tid] = tid < nq ? a.gsrc[it.goff + tid] : base;
       s_dst[tid] = tid < nq ? a.gdst[it.goff + tid] : -1;
+      if (!LAYA_IN_BOUNDS(a.rows <= 0 || (s_src[tid] >= base && s_src[tid] < base + len &&
+                                          s_dst[tid] < (a.rows_out > 0 ? a.rows_out : a.rows)),
+                          a.err, kErrBoundsGather)) {
+        s_src[tid] = base;  // the query reads its sequence's first row and its output is dropped
+        s_dst[tid] = -1;
+      }
     }
     __syncthreads();
   } else {
@@ -229,7 +240,7 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const AttnArgs a) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int id = lane + 32 * i, r = warp * 16 + (id >> 3), c = id & 7;
-    if (r < nq) {
+    if (r < nq && (!GATHER || s_dst[r] >= 0)) {  // s_dst < 0: dropped by a debug bounds check
       const long long dst = GATHER ? (long long)s_dst[r] : (long long)base + it.q0 + r;
       *reinterpret_cast<uint4*>(out + dst * D + h * 64 + c * 8) = *reinterpret_cast<const uint4*>(sQ + swz(r, c));
     }
@@ -244,12 +255,24 @@ __global__ void __launch_bounds__(64) attn_f32_kernel(const AttnArgs a) {
   pdl_wait();
   const AttnItem it = a.items[blockIdx.x];
   if (it.seq < 0) return;
+  if (!LAYA_IN_BOUNDS(a.n_seq <= 0 || it.seq < a.n_seq, a.err, kErrBoundsAttn)) return;
   const int h = blockIdx.y, D = a.H * 64, tid = threadIdx.x;
   const long long ld = 3LL * D;
   const int base = a.soff[it.seq], len = a.slen[it.seq];
+  if (!LAYA_IN_BOUNDS(a.rows <= 0 || (base >= 0 && len > 0 && base + len <= a.rows &&
+                                      (GATHER ? (it.nq >= 1 && it.nq <= 64) : (it.q0 >= 0 && it.q0 < len))),
+                      a.err, kErrBoundsAttn))
+    return;
   const float* qkv = static_cast<const float*>(a.qkv);
   const int nq = GATHER ? it.nq : min(64, len - it.q0);
-  const bool qv = tid < nq;
+  bool qv = tid < nq;
+  if (GATHER && qv) {
+    const int gs = a.gsrc[it.goff + tid], gd = a.gdst[it.goff + tid];
+    if (!LAYA_IN_BOUNDS(a.rows <= 0 || (gs >= base && gs < base + len && gd >= 0 &&
+                                        gd < (a.rows_out > 0 ? a.rows_out : a.rows)),
+                        a.err, kErrBoundsGather))
+      qv = false;
+  }
   const long long qrow = GATHER ? (qv ? (long long)a.gsrc[it.goff + tid] : base)
                                 : (long long)base + it.q0 + (qv ? tid : 0);
   const int qpos = GATHER ? 0 : it.q0 + tid;

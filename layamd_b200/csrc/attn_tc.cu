@@ -165,6 +165,11 @@ __device__ __forceinline__ bool unit_of(const AttnArgs& a, int w, int nwork, Uni
   if (w >= nwork) return false;
   const int4 it = __ldg(reinterpret_cast<const int4*>(a.items) + w / a.H);
   if (it.x < 0) return false;
+  // debug bounds mode: a unit whose rows fall outside qkv is dropped (as if it were past the end)
+  if (!LAYA_IN_BOUNDS(a.rows <= 0 || (it.z >= 0 && it.w > 0 && it.z + it.w <= a.rows && it.y >= 0 && it.y < it.w &&
+                                      (a.n_seq <= 0 || it.x < a.n_seq)),
+                      a.err, kErrBoundsAttn))
+    return false;
   u.h = w % a.H;
   u.q0 = it.y;
   u.base = it.z;

@@ -23,6 +23,13 @@ enum DevErr : int {
   kErrAttnMma = 17,      // attention MMA issuer timed out waiting for Q / K / V / P
   kErrAttnSoftmax = 18,  // attention softmax warps timed out waiting for S or O
   kErrSelfTest = 30,     // watchdog self-test: a wait on a barrier phase that nothing completes
+  // debug bounds mode (LAYA_DEBUG_BOUNDS builds): an index read from the packing maps is out of range
+  kErrBoundsLnSrc = 40,    // LayerNorm source row (token id / gathered row) beyond its table
+  kErrBoundsLnSeq = 41,    // LayerNorm row -> question or question type out of range
+  kErrBoundsRope = 42,     // GEMM RoPE position beyond the cos / sin tables
+  kErrBoundsAttn = 43,     // attention work item: sequence, rows or query block out of range
+  kErrBoundsGather = 44,   // gathered attention: source or destination row out of range
+  kErrBoundsHead = 45,     // decision-head outputs: marker rows or logit slots out of range
 };
 
 // ---------------------------------------------------------------- programmatic dependent launch
@@ -117,6 +124,19 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Debug bounds mode. Built with -DLAYA_DEBUG_BOUNDS, LAYA_IN_BOUNDS(cond, err, code) records `code`
+// in the error word (first writer wins) and yields false when `cond` fails, so the caller skips the
+// access instead of reading or writing out of range; in normal builds it is `true` and costs nothing.
+__device__ __forceinline__ bool bounds_fail(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+  return false;
+}
+#ifdef LAYA_DEBUG_BOUNDS
+#define LAYA_IN_BOUNDS(cond, err, code) ((cond) ? true : ::laya::bounds_fail((err), (code)))
+#else
+#define LAYA_IN_BOUNDS(cond, err, code) true
+#endif
+
 // Bounded wait on phase `parity`. Returns false (after recording `code`) when the budget runs out
 // or when another role of the CTA has already aborted (`*abort` set).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,

@@ -113,6 +113,139 @@ bool plan_passes(int B, const int* lens, const int* nmark, int pass_tokens, int 
   return true;
 }
 
+void fill_pass_meta(const PassPlan& p, const Question* qs, int pad_id, int* m) {
+  const MetaLayout L = meta_layout(p.Tpad, p.n, p.R);
+  AttnItem* items = reinterpret_cast<AttnItem*>(m + L.items);
+  AttnItem* items128 = reinterpret_cast<AttnItem*>(m + L.items128);
+  AttnItem* gitems = reinterpret_cast<AttnItem*>(m + L.gitems);
+  int r = 0, mo = 0, it = 0, it128 = 0, git = 0, gl = 0;
+  for (int i = 0; i < p.n; ++i) {
+    const Question& q = qs[p.b0 + i];
+    m[L.soff + i] = r;
+    m[L.slen + i] = q.len;
+    m[L.qt + i] = q.qtype;
+    m[L.nm + i] = q.nmark;
+    m[L.moff + i] = mo;
+    memcpy(m + L.ids + r, q.ids, (size_t)q.len * 4);
+    for (int j = 0; j < q.len; ++j) {
+      m[L.pos + r + j] = j;
+      m[L.rowseq + r + j] = i;
+    }
+    for (int q0 = 0; q0 < q.len; q0 += 64) items[it++] = AttnItem{i, q0, 0, 0};
+    for (int q0 = 0; q0 < q.len; q0 += 128) items128[it128++] = AttnItem{i, q0, r, q.len};  // base row, length
+    const int cnt = q.nmark + 1;
+    for (int k = 0; k < q.nmark; ++k) {
+      m[L.gsrc + gl + k] = r + q.markers[k];
+      m[L.gdst + gl + k] = mo + k;
+      m[L.grow + mo + k] = r + q.markers[k];
+    }
+    m[L.gsrc + gl + q.nmark] = r;
+    m[L.gdst + gl + q.nmark] = p.KT + i;
+    m[L.grow + p.KT + i] = r;
+    for (int c0 = 0; c0 < cnt; c0 += 64) gitems[git++] = AttnItem{i, 0, gl + c0, std::min(64, cnt - c0)};
+    gl += cnt;
+    r += q.len;
+    mo += q.nmark;
+  }
+  for (int j = r; j < p.Tpad; ++j) {
+    m[L.ids + j] = pad_id;
+    m[L.pos + j] = 0;
+    m[L.rowseq + j] = -1;
+  }
+  // the persistent tcgen05 attention deals its units out round robin: longest sequences first
+  std::stable_sort(items128, items128 + it128, [](const AttnItem& a, const AttnItem& b) { return a.nq > b.nq; });
+  for (; it < L.items_cap; ++it) items[it] = AttnItem{-1, 0, 0, 0};
+  for (; it128 < L.items128_cap; ++it128) items128[it128] = AttnItem{-1, 0, 0, 0};
+  for (; git < L.gitems_cap; ++git) gitems[git] = AttnItem{-1, 0, 0, 0};
+}
+
+size_t pass_meta_ints(const PassPlan& p) { return meta_layout(p.Tpad, p.n, p.R).total; }
+
+void corrupt_pass_meta(const PassPlan& p, int* m, int which, int vocab) {
+  const MetaLayout L = meta_layout(p.Tpad, p.n, p.R);
+  const int last = p.n - 1;
+  switch (which) {
+    case 1: m[L.soff + last] += 1; break;                         // question offset
+    case 2: m[L.qt + last] = 3; break;                            // question type
+    case 3: m[L.nm + last] = kMaxMarkers + 1; break;              // marker count
+    case 4: m[L.ids + p.T - 1] = vocab; break;                    // token id past the vocabulary
+    case 5: m[L.rowseq + p.T - 1] = p.n; break;                   // row -> question
+    case 6: reinterpret_cast<AttnItem*>(m + L.items)[0].q0 = 64 * ((m[L.slen] + 63) / 64); break;  // 64-row item
+    case 7: m[L.gsrc + 0] = m[L.soff] + m[L.slen]; break;         // gathered query outside its question
+    case 8: m[L.grow + p.R - 1] = p.T; break;                     // gathered row past the packed rows
+    default: break;
+  }
+}
+
+int check_pass_meta(const PassPlan& p, const int* m, const PackLimits& lim) {
+  const MetaLayout L = meta_layout(p.Tpad, p.n, p.R);
+  if (p.n < 1 || p.n > lim.max_seqs || p.Tpad > lim.max_rows || p.Tpad % 64 != 0 || p.T > p.Tpad ||
+      p.R != p.KT + p.n || p.R > lim.max_gathered)
+    return 1;  // pass shape beyond the arena
+  const int *ids = m + L.ids, *pos = m + L.pos, *rowseq = m + L.rowseq, *soff = m + L.soff, *slen = m + L.slen,
+            *qt = m + L.qt, *nm = m + L.nm, *moff = m + L.moff, *gsrc = m + L.gsrc, *gdst = m + L.gdst,
+            *grow = m + L.grow;
+  int r = 0, mo = 0;
+  for (int i = 0; i < p.n; ++i) {  // questions back to back, in order
+    if (soff[i] != r || slen[i] < 1 || slen[i] > lim.max_len) return 2;
+    if (qt[i] < 0 || qt[i] > 2) return 3;
+    if (nm[i] < 1 || nm[i] > kMaxMarkers || moff[i] != mo) return 4;
+    r += slen[i];
+    mo += nm[i];
+  }
+  if (r != p.T || mo != p.KT) return 5;
+  for (int j = 0; j < p.Tpad; ++j) {  // per-row maps
+    if (ids[j] < 0 || ids[j] >= lim.vocab) return 6;
+    const int s = rowseq[j];
+    if (j < p.T ? (s < 0 || s >= p.n || j < soff[s] || j >= soff[s] + slen[s] || pos[j] != j - soff[s])
+                : (s != -1 || pos[j] != 0))
+      return 7;
+  }
+  // every row of every question in exactly one query block: a question's blocks are adjacent in the
+  // list, in order, starting at 0 and ending at its last row; unused slots only after the last block
+  auto items_ok = [&](const AttnItem* it, int cap, int rows_per, bool tc) {
+    std::vector<char> done(p.n, 0);
+    int cur = -1, next_q0 = 0, used = 0;
+    for (int k = 0; k < cap; ++k) {
+      const int s = it[k].seq;
+      if (s < 0) break;
+      ++used;
+      if (s >= p.n || (tc && (it[k].goff != soff[s] || it[k].nq != slen[s]))) return false;
+      if (s != cur) {
+        if (cur >= 0 && next_q0 < slen[cur]) return false;  // the previous question is incomplete
+        if (done[s]) return false;
+        done[s] = 1;
+        cur = s;
+        next_q0 = 0;
+      }
+      if (it[k].q0 != next_q0 || next_q0 >= slen[s]) return false;
+      next_q0 += rows_per;
+    }
+    for (int k = used; k < cap; ++k)
+      if (it[k].seq >= 0) return false;
+    if (cur < 0 || next_q0 < slen[cur]) return false;
+    for (int i = 0; i < p.n; ++i)
+      if (!done[i]) return false;
+    return true;
+  };
+  if (!items_ok(reinterpret_cast<const AttnItem*>(m + L.items), L.items_cap, 64, false)) return 8;
+  if (!items_ok(reinterpret_cast<const AttnItem*>(m + L.items128), L.items128_cap, 128, true)) return 9;
+  const AttnItem* g = reinterpret_cast<const AttnItem*>(m + L.gitems);
+  long long gl = 0;
+  for (int k = 0; k < L.gitems_cap; ++k) {  // gathered queries: markers then the CLS row
+    if (g[k].seq < 0) continue;
+    const int s = g[k].seq;
+    if (s >= p.n || g[k].nq < 1 || g[k].nq > 64 || g[k].goff != gl || g[k].goff + g[k].nq > p.R) return 10;
+    for (int t = g[k].goff; t < g[k].goff + g[k].nq; ++t)
+      if (gsrc[t] < soff[s] || gsrc[t] >= soff[s] + slen[s] || gdst[t] < 0 || gdst[t] >= p.R) return 11;
+    gl += g[k].nq;
+  }
+  if (gl != p.R) return 12;
+  for (int t = 0; t < p.R; ++t)
+    if (grow[t] < 0 || grow[t] >= p.T) return 13;
+  return 0;
+}
+
 // ===================================================================== Replica (one GPU)
 class Replica {
  public:
@@ -194,6 +327,7 @@ class Replica {
   // Failure injection for host-side tests (LAYA_FAIL_REPLICA=i[:n] at load): this replica's next
   // n non-empty shards return -2 before anything is uploaded or launched.
   int fail_runs = 0;
+  int plant_id = 0;  // debug-bounds builds: LAYA_DEBUG_PLANT_ID test hook (see fill)
 
   Replica(Engine& e, int d) : E(e), cfg(e.cfg), dev(d) {}
   ~Replica() { release(); }
@@ -426,52 +560,30 @@ class Replica {
   }
 
   // ------------------------------------------------------------------ one pass
-  // Fills the pinned staging block for pass `p` of `qs`.
+  // Fills the pinned staging block for pass `p` of `qs` (and checks it in debug bounds mode).
+  bool pack_ok = true;
   void fill(const PassPlan& p, const Question* qs) {
-    const MetaLayout L = meta_layout(p.Tpad, p.n, p.R);
-    int* m = h_meta;
-    AttnItem* items = reinterpret_cast<AttnItem*>(m + L.items);
-    AttnItem* items128 = reinterpret_cast<AttnItem*>(m + L.items128);
-    AttnItem* gitems = reinterpret_cast<AttnItem*>(m + L.gitems);
-    int r = 0, mo = 0, it = 0, it128 = 0, git = 0, gl = 0;
-    for (int i = 0; i < p.n; ++i) {
-      const Question& q = qs[p.b0 + i];
-      m[L.soff + i] = r;
-      m[L.slen + i] = q.len;
-      m[L.qt + i] = q.qtype;
-      m[L.nm + i] = q.nmark;
-      m[L.moff + i] = mo;
-      memcpy(m + L.ids + r, q.ids, (size_t)q.len * 4);
-      for (int j = 0; j < q.len; ++j) {
-        m[L.pos + r + j] = j;
-        m[L.rowseq + r + j] = i;
+    fill_pass_meta(p, qs, cfg.pad_id, h_meta);
+    pack_ok = true;
+    if (E.debug_bounds) {
+      PackLimits lim{cfg.vocab, cfg.max_len, Tcap, Rcap, Bcap};
+      const int bad = check_pass_meta(p, h_meta, lim);
+      if (bad) {
+        fprintf(stderr, "[laya] device %d: packing check %d failed for a pass of %d questions (debug bounds mode)\n",
+                dev, bad, p.n);
+        pack_ok = false;
       }
-      for (int q0 = 0; q0 < q.len; q0 += 64) items[it++] = AttnItem{i, q0, 0, 0};
-      for (int q0 = 0; q0 < q.len; q0 += 128) items128[it128++] = AttnItem{i, q0, r, q.len};  // base row, length
-      const int cnt = q.nmark + 1;
-      for (int k = 0; k < q.nmark; ++k) {
-        m[L.gsrc + gl + k] = r + q.markers[k];
-        m[L.gdst + gl + k] = mo + k;
-        m[L.grow + mo + k] = r + q.markers[k];
-      }
-      m[L.gsrc + gl + q.nmark] = r;
-      m[L.gdst + gl + q.nmark] = p.KT + i;
-      m[L.grow + p.KT + i] = r;
-      for (int c0 = 0; c0 < cnt; c0 += 64) gitems[git++] = AttnItem{i, 0, gl + c0, std::min(64, cnt - c0)};
-      gl += cnt;
-      r += q.len;
-      mo += q.nmark;
     }
-    for (int j = r; j < p.Tpad; ++j) {
-      m[L.ids + j] = cfg.pad_id;
-      m[L.pos + j] = 0;
-      m[L.rowseq + j] = -1;
+#ifdef LAYA_DEBUG_BOUNDS
+    // Test hook of debug-bounds builds only (LAYA_DEBUG_PLANT_ID=n at load): the next n passes get a
+    // token id one past the vocabulary after the host check, so the embedding kernel's own bounds
+    // check must catch it on the device (code 40). The row it would read lies inside the table's
+    // allocation granule, so even a missing check could not fault.
+    if (plant_id > 0) {
+      --plant_id;
+      h_meta[meta_layout(p.Tpad, p.n, p.R).ids + p.T - 1] = cfg.vocab;
     }
-    // the persistent tcgen05 attention deals its units out round robin: longest sequences first
-    std::stable_sort(items128, items128 + it128, [](const AttnItem& a, const AttnItem& b) { return a.nq > b.nq; });
-    for (; it < L.items_cap; ++it) items[it] = AttnItem{-1, 0, 0, 0};
-    for (; it128 < L.items128_cap; ++it128) items128[it128] = AttnItem{-1, 0, 0, 0};
-    for (; git < L.gitems_cap; ++git) gitems[git] = AttnItem{-1, 0, 0, 0};
+#endif
   }
 
   cudaError_t first_err = cudaSuccess;
@@ -607,11 +719,18 @@ class Replica {
     a.D = cfg.d;
     a.eps = cfg.norm_eps;
     a.out_planes = P;
+    a.err = d_err;
     return a;
   }
+  // extents of the current pass for the debug bounds checks of the attention kernels
+  int pass_rows = 0, pass_rows_out = 0, pass_seqs = 0;
   void attend(const AttnItem* items, int n_items, const int* soff, const int* slen, int window, void* out,
               long long out_plane, const int* gsrc, const int* gdst) {
     AttnArgs a;
+    a.rows = pass_rows;
+    a.rows_out = gsrc ? pass_rows_out : pass_rows;
+    a.n_seq = pass_seqs;
+    a.err = d_err;
     a.qkv = qkv;
     a.out = out;
     a.out_plane = out_plane;
@@ -638,6 +757,10 @@ class Replica {
       return;
     }
     AttnArgs a;
+    a.rows = pass_rows;
+    a.rows_out = pass_rows;
+    a.n_seq = pass_seqs;
+    a.err = d_err;
     a.qkv = qkv;
     a.out = ao.p;
     a.out_plane = ao.plane;
@@ -679,6 +802,9 @@ class Replica {
     const AttnItem* items128 = reinterpret_cast<const AttnItem*>(dm + L.items128);
     const AttnItem* gitems = reinterpret_cast<const AttnItem*>(dm + L.gitems);
     const int qkv_mode = P == 2 ? OUT_F32 : OUT_BF16;
+    pass_rows = M;
+    pass_rows_out = R;
+    pass_seqs = p.n;
     char nb[32];
     if (h2d) stage("h2d", [&] { chk(cudaMemcpyAsync(d_meta, h_meta, L.total * 4, cudaMemcpyHostToDevice, st)); });
 
@@ -686,6 +812,7 @@ class Replica {
       LnArgs a = ln_base(M);
       a.src = tok_emb;
       a.ids = ids;
+      a.src_rows = cfg.vocab;
       a.w = emb_norm;
       a.out_f32 = x;
       a.out_bf = xn.p;
@@ -704,6 +831,7 @@ class Replica {
         e.sin_t = glob ? sin_g : sin_l;
         e.pos = pos;
         e.rope_cols = 2 * D;
+        e.rope_rows = cfg.max_len;
         gemm(xn, M, enc[l].Wqkv, out_qkv, qkv, 0, e);
       });
       stage(glob ? "attn_global" : "attn_sliding", [&] {
@@ -743,6 +871,7 @@ class Replica {
           a.type_emb = type_emb;
           a.qtype = qt;
           a.rowseq = rowseq;
+          a.n_seq = p.n;
           a.out_f32 = x;
           a.w2 = head[0].n1w;
           a.b2 = head[0].n1b;
@@ -790,6 +919,7 @@ class Replica {
           LnArgs a = ln_base(R);
           a.src = x;
           a.gidx = grow;
+          a.src_rows = M;
           a.out_f32 = xg;
           launched(ln_launch(a, st));
         });
@@ -839,6 +969,8 @@ class Replica {
       a.b2 = a2B;
       a.logits = d_logits;
       a.act = d_act;
+      a.n_logits = KT;
+      a.err = d_err;
       launched(head_out_launch(a, st));
     });
     if (d2h) {
@@ -934,6 +1066,7 @@ class Replica {
     if (!plan_passes((int)qs.size(), lens.data(), nms.data(), E.pass_tokens, Bcap, Rcap, &plans)) return -1;
     for (const PassPlan& p : plans) {
       fill(p, qs.data());
+      if (!pack_ok) return -3;
       const int rc = execute(p);
       if (rc) return rc;
       scatter(p, qs.data());
@@ -955,6 +1088,7 @@ class Replica {
     if (plans.size() != 1) return -3;  // the staged batch must be one pass
     staged_plan = plans[0];
     fill(staged_plan, staged.data());
+    if (!pack_ok) return -3;
     first_err = cudaSuccess;
     chk(cudaMemcpyAsync(d_meta, h_meta, meta_layout(staged_plan.Tpad, staged_plan.n, staged_plan.R).total * 4,
                         cudaMemcpyHostToDevice, st));
@@ -1125,6 +1259,9 @@ bool Engine::load(const std::string& dir, int prec, const std::string& devices, 
   cudaSetDevice(prev);
   for (size_t i = 0; i < devs.size(); ++i)
     if (!ok[i]) { *err = "device " + std::to_string(devs[i]) + ": " + errs[i]; return false; }
+  debug_bounds = kDebugBoundsBuild || env_int("LAYA_DEBUG_BOUNDS", 0) != 0;
+  if (kDebugBoundsBuild)
+    for (auto& r : reps) r->plant_id = env_int("LAYA_DEBUG_PLANT_ID", 0);
   if (const char* f = getenv("LAYA_FAIL_REPLICA")) {
     const int i = atoi(f);
     const char* c = strchr(f, ':');
@@ -1269,9 +1406,21 @@ std::vector<std::vector<Question>> Engine::shard(int B, const int* lens, const i
   return out;
 }
 
+bool validate_tokens(int B, const int* lens, const int* ids, const int* qtypes, int vocab) {
+  size_t nt = 0;
+  for (int b = 0; b < B; ++b) {
+    if (qtypes[b] < 0 || qtypes[b] > 2) return false;
+    nt += lens[b];
+  }
+  for (size_t t = 0; t < nt; ++t)
+    if (ids[t] < 0 || ids[t] >= vocab) return false;
+  return true;
+}
+
 int Engine::forward_batch(int B, const int* lens, const int* ids, const int* nmark, const int* markers,
                           const int* qtypes, float* logits, float* act) {
   if (!validate_batch(B, lens, nmark, markers, cfg.max_len)) return -1;
+  if (!validate_tokens(B, lens, ids, qtypes, cfg.vocab)) return -1;
   if (B == 0) return 0;
   auto shards = shard(B, lens, ids, nmark, markers, qtypes, logits, act);
   if (reps.size() == 1) return reps[0]->run(shards[0]);
@@ -1280,6 +1429,7 @@ int Engine::forward_batch(int B, const int* lens, const int* ids, const int* nma
 
 int Engine::stage(int B, const int* lens, const int* ids, const int* nmark, const int* markers, const int* qtypes) {
   if (!validate_batch(B, lens, nmark, markers, cfg.max_len)) return -1;
+  if (!validate_tokens(B, lens, ids, qtypes, cfg.vocab)) return -1;
   // keep private copies: the staged pass replays them
   size_t nt = 0, nk = 0;
   for (int b = 0; b < B; ++b) { nt += lens[b]; nk += nmark[b]; }

@@ -49,6 +49,27 @@ bool plan_passes(int B, const int* lens, const int* nmark, int pass_tokens, int 
 // marker count in [1, 255], every marker inside its sequence.
 bool validate_batch(int B, const int* lens, const int* nmark, const int* markers, int max_len);
 
+// Limits a pass's metadata must respect (the arena it is uploaded into and the model's tables).
+struct PackLimits {
+  int vocab, max_len;
+  int max_rows, max_gathered, max_seqs;
+};
+
+// Ints of pass `p`'s metadata block.
+size_t pass_meta_ints(const PassPlan& p);
+
+// Test hook of laya_pack_check: breaks map number `which` (1-8: question offset, question type,
+// marker count, token id, row -> question, 64-row item, gathered source row, gathered row) of a filled
+// block, so that a test can show that check_pass_meta catches it. Host memory only.
+void corrupt_pass_meta(const PassPlan& p, int* m, int which, int vocab);
+
+// True in builds compiled with -DLAYA_DEBUG_BOUNDS (device-side index checks in every kernel).
+#ifdef LAYA_DEBUG_BOUNDS
+constexpr bool kDebugBoundsBuild = true;
+#else
+constexpr bool kDebugBoundsBuild = false;
+#endif
+
 // Model dimensions the shard cost model needs (a subset of Config, so host-only callers can pass
 // them by value).
 struct ShardModel {
@@ -65,6 +86,10 @@ ShardModel shard_model(const Config& c);
 // 175, so the weights are 4 (GEMM), 14 (global / head attention) and 26 (sliding attention) per FLOP.
 // Integer arithmetic, so that a restatement reproduces the assignment exactly.
 long long question_cost(const ShardModel& m, int L, int k);
+
+// Token ids inside [0, vocab) and question types 0..2 (an addition to the reference's validation,
+// whose embedding gather would read outside its table for such an id).
+bool validate_tokens(int B, const int* lens, const int* ids, const int* qtypes, int vocab);
 
 // Replica of each question when a call is sharded over G replicas: longest processing time first
 // (question_cost, descending; ties in input order) onto the least-loaded replica (lowest index on a
@@ -91,6 +116,17 @@ struct Question {  // one question of the caller's batch, by reference into the 
   float* logits;  // destination of its nmark logits
   float* act;     // destination of its n_act act logits
 };
+
+// Fills the per-pass metadata block (token ids, positions, row -> question map, per-question offsets,
+// lengths, types and marker offsets, the three attention work-item lists and the gathered-row maps)
+// for pass `p` of `qs` into `m` (meta_layout order).
+void fill_pass_meta(const PassPlan& p, const Question* qs, int pad_id, int* m);
+
+// Debug bounds mode, host side: checks every map of a filled metadata block against the pass and
+// `lim` (ids inside the vocabulary, rows inside their question, work items covering every row once,
+// gathered rows inside their question and the gathered buffer, ...). Returns 0, or the number of the
+// first check that failed (1-13).
+int check_pass_meta(const PassPlan& p, const int* m, const PackLimits& lim);
 
 class Replica;
 
@@ -121,6 +157,9 @@ class Engine {
   int max_tokens = 131072, pass_tokens = 131072, max_seqs = 4096, max_gathered = 0;
   bool use_graphs = true;
   bool prof_on = false;
+  // debug bounds mode (LAYA_DEBUG_BOUNDS=1, or a debug-bounds build): every pass's metadata is checked
+  // on the host before it is uploaded (check_pass_meta); a failed check returns -3 without launching
+  bool debug_bounds = false;
   std::string dump_dir;
   std::vector<std::unique_ptr<Replica>> reps;
   // workers[i] runs replica i's part of a call for i >= 1; replica 0 runs on the caller's thread

@@ -166,7 +166,8 @@ __device__ __forceinline__ void epilogue_tile(const Loader& ld, int row0, int la
     float cs[32], sn[32];
     const bool any_rot = nb * BN < ep.rope_cols;
     if (any_rot && valid) {
-      const int p = ep.pos[row];
+      int p = ep.pos[row];
+      if (!LAYA_IN_BOUNDS(ep.rope_rows <= 0 || (p >= 0 && p < ep.rope_rows), ep.err, kErrBoundsRope)) p = 0;
       const float4* ct = reinterpret_cast<const float4*>(ep.cos_t + (size_t)p * 32);
       const float4* st = reinterpret_cast<const float4*>(ep.sin_t + (size_t)p * 32);
 #pragma unroll
@@ -464,7 +465,8 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmShape sh, 
     }
     if constexpr (EPI == EPI_ROPE) {
       if (c0 < ep.rope_cols) {
-        const long long p = ep.pos[row];
+        long long p = ep.pos[row];
+        if (!LAYA_IN_BOUNDS(ep.rope_rows <= 0 || (p >= 0 && p < ep.rope_rows), ep.err, kErrBoundsRope)) p = 0;
         const float4 cs = *reinterpret_cast<const float4*>(ep.cos_t + p * 32 + 4 * t);
         const float4 sn = *reinterpret_cast<const float4*>(ep.sin_t + p * 32 + 4 * t);
         const float4 ra = make_float4(a.x * cs.x - b.x * sn.x, a.y * cs.y - b.y * sn.y, a.z * cs.z - b.z * sn.z,
@@ -833,8 +835,10 @@ cudaError_t gemm_prepare_device() {
 }
 
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, int bn,
-                        const GemmShape& sh, const GemmEpi& ep, int* err, int grid_ctas, cudaStream_t st) {
+                        const GemmShape& sh, const GemmEpi& ep_in, int* err, int grid_ctas, cudaStream_t st) {
   if (sh.M <= 0) return cudaSuccess;
+  GemmEpi ep = ep_in;
+  ep.err = err;
   if (sh.splits > 1 && (bn == kGemmPair || !sh.ws || !sh.dst || sh.splits > kMaxSplits ||
                         (reinterpret_cast<uintptr_t>(sh.ws) & 15) != 0 || (reinterpret_cast<uintptr_t>(sh.dst) & 15) != 0 ||
                         (ep.out_mode == OUT_BF16X2 && ep.kind != EPI_RESID && sh.dst_plane % 4 != 0)))

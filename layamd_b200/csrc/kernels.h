@@ -83,6 +83,10 @@ struct GemmEpi {
   bf16* ln_out = nullptr;
   long long ln_plane = 0;
   int ln_planes = 1;
+  // debug bounds mode: rows of the RoPE tables (positions must lie below it) and the error word
+  // (gemm_launch fills it from its `err`)
+  int rope_rows = 0;
+  int* err = nullptr;
 };
 
 // Output map of the GEMM epilogue over [planes][rows][ld] (bf16) or [rows][ld] (fp32, planes 1):
@@ -171,6 +175,11 @@ struct AttnArgs {
   int H;                 // heads (head dim is 64)
   int window;            // half window (|q-k| <= window), 0 = global
   float scale;           // softmax scale (1/sqrt(64))
+  // extents the debug bounds mode checks the maps against (0: unchecked), and its error word
+  int rows = 0;          // rows of qkv
+  int rows_out = 0;      // rows of out
+  int n_seq = 0;         // entries of soff / slen
+  int* err = nullptr;
 };
 cudaError_t attn_bf16_launch(const AttnArgs& a, cudaStream_t st);
 cudaError_t attn_f32_launch(const AttnArgs& a, cudaStream_t st);
@@ -209,6 +218,10 @@ struct LnArgs {
   bf16* out_bf = nullptr;         // write (second LN ? z : y) as bf16 planes
   int out_planes = 1;
   long long out_plane = 0;
+  // extents the debug bounds mode checks the maps against (0: unchecked), and its error word
+  int src_rows = 0;               // rows of src that ids / gidx may name
+  int n_seq = 0;                  // entries of qtype that rowseq may name
+  int* err = nullptr;
 };
 cudaError_t ln_launch(const LnArgs& a, cudaStream_t st);
 
@@ -229,6 +242,9 @@ struct HeadOutArgs {
   const float* b2 = nullptr;
   float* logits = nullptr;        // [sum nmark]
   float* act = nullptr;           // [B, n_act]
+  // extents the debug bounds mode checks the maps against (0: unchecked), and its error word
+  int n_logits = 0;               // marker rows of hs / logit slots
+  int* err = nullptr;
 };
 cudaError_t head_out_launch(const HeadOutArgs& a, cudaStream_t st);
 

@@ -29,6 +29,7 @@ __global__ void __launch_bounds__(256) ln_kernel(const LnArgs a) {
   if (row >= a.rows) return;
   const int D = a.D;
   const long long src_row = a.ids ? (long long)a.ids[row] : a.gidx ? (long long)a.gidx[row] : (long long)row;
+  if (!LAYA_IN_BOUNDS(a.src_rows <= 0 || (src_row >= 0 && src_row < a.src_rows), a.err, kErrBoundsLnSrc)) return;
   const float4* src = reinterpret_cast<const float4*>(a.src + src_row * D);
   float4 v[NV];
 #pragma unroll
@@ -42,7 +43,8 @@ __global__ void __launch_bounds__(256) ln_kernel(const LnArgs a) {
     layer_norm_regs<NV>(v, a.w, a.b, a.eps, D, lane);
     if (a.type_emb) {
       const int s = a.rowseq[row];
-      if (s >= 0) {
+      if (s >= 0 && LAYA_IN_BOUNDS((a.n_seq <= 0 || s < a.n_seq) && a.qtype[s] >= 0 && a.qtype[s] < 3, a.err,
+                                   kErrBoundsLnSeq)) {
         const float4* t = reinterpret_cast<const float4*>(a.type_emb + (long long)a.qtype[s] * D);
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
@@ -110,6 +112,9 @@ __global__ void __launch_bounds__(256) head_out_kernel(const HeadOutArgs a) {
   pdl_wait();
   const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int D = a.D, nm = a.nmark[b], mo = a.moff[b];
+  if (!LAYA_IN_BOUNDS(nm >= 1 && nm <= 256 && mo >= 0 && (a.n_logits <= 0 || mo + nm <= a.n_logits), a.err,
+                      kErrBoundsHead))
+    return;
   // scorer output Linear(d, 1) at every option marker of this question, one warp per marker
   for (int k = warp; k < nm; k += 8) {
     const long long row = mo + k;
