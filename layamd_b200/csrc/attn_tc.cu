@@ -435,6 +435,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         // raise the reference max only when it grows by more than 2^8 (p stays <= 256 otherwise)
         const float m_new = fmaxf(m_used, mx);
         const bool resc = m_new > m_used + 8.f;
+        // O (and l) hold something to rescale only once a key of this row has been visible: until
+        // then every P of the row was 0, so its O row is exactly 0 (and the V rows are finite)
+        const bool resc_o = resc && m_used != -INFINITY;
         float alpha = 1.f;
         if (resc) {
           alpha = ex2(m_used - m_new);  // 0 on the first visible chunk (m_used = -inf)
@@ -460,8 +463,9 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
           }
         }
-        // O may only be rescaled once the PV in flight (chunk c-1) has landed
-        if (j > 0 && __any_sync(0xffffffffu, resc)) {
+        // O may only be rescaled once the PV in flight (chunk c-1) has landed; a row's first visible
+        // chunk needs no rescale
+        if (j > 0 && __any_sync(0xffffffffu, resc_o)) {
           if (!mbar_wait(smem_u32(&S.pfree[(c - 1) & 1]), ((c - 1) >> 1) & 1, abort, err, kErrAttnSoftmax)) {
             ok = false;
             break;
