@@ -6,8 +6,10 @@ kernel through the C ABI entry point ``laya_b200_gemm`` with CUDA events (warm-u
 back launches on one stream), in bf16 (one bf16 product, fp32 accumulation) and in fp32-parity mode
 (three bf16 products on hi/lo splits). Inputs: A ~ N(0,1), W ~ N(0,0.02), seed 5. Reports TFLOP/s
 (2MNK/t, parity mode counted as the same 2MNK), the fraction of the measured sustained and burst bf16
-peaks, the tile the engine would pick, torch.matmul (cuBLAS) on the same bf16 operands as a
-comparator, and max|C - C_ref| / max|C_ref| against an fp64 reference GEMM of the fp32 inputs.
+peaks, the engine's plan for the shape (tile and K split; split shapes run through
+``laya_b200_gemm_splitk``), torch.matmul (cuBLAS) on the same bf16 operands as a
+comparator, and max|C - C_ref| / max|C_ref| against an fp64 reference GEMM of the fp32 inputs. The
+bf16 rows write fp32 for that check; ``--no-check`` writes bf16 as cuBLAS does (like-for-like timing).
 
 Usage: python -m layamd_b200.gemm_sweep [--m 512,4096] [--kn 1024x3072,...] [--epi store|geglu|rope|resid]
        [--modes bf16,parity] [--tile auto|128|256|pair] [--iters 20] [--no-check] [--json]
@@ -32,13 +34,13 @@ def peaks():
         return 1400.0, 1590.0
 
 
-def pick_tile(L, M, N, K, sms):
-    """The engine's tile for this shape (laya_plan_gemm: the CTA-pair 256 x 256 tile when its tiles
-    fill every co-resident pair twice, else the width with fewer whole waves); this sweep never splits
-    K, so only the tile is taken."""
+def plan(L, M, N, K, sms, parity):
+    """The engine's plan for this shape (laya_plan_gemm): the tile (the CTA-pair 256 x 256 tile when
+    its tiles fill every co-resident pair twice, else the width with fewer whole waves) and the K
+    split (slices for a few hundred rows of long K, where 128 x 128 tiles cannot fill the GPU)."""
     bn, splits = ctypes.c_int(0), ctypes.c_int(0)
-    assert L.laya_plan_gemm(M, N, K, 0, sms, sms // 2, 0, ctypes.byref(bn), ctypes.byref(splits)) == 0
-    return bn.value
+    assert L.laya_plan_gemm(M, N, K, parity, sms, sms // 2, 0, ctypes.byref(bn), ctypes.byref(splits)) == 0
+    return bn.value, splits.value
 
 
 def interleave_geglu(W, I):
@@ -82,12 +84,16 @@ def main():
             if epi == EPI["geglu"]:
                 W32 = interleave_geglu(W32, I)
             ncols = I if epi == EPI["geglu"] else N
-            bn = pick_tile(L, M, N, K, sms) if a.tile == "auto" else TILES[a.tile]
+
             pos = torch.randint(0, 512, (M,), device=dev, dtype=torch.int32, generator=g)
             cos = torch.rand(512, 32, device=dev)
             sin = torch.rand(512, 32, device=dev)
             for mode in a.modes.split(","):
                 planes = 2 if mode == "parity" else 1
+                if a.tile == "auto":
+                    bn, splits = plan(L, M, N, K, sms, planes == 2)
+                else:
+                    bn, splits = TILES[a.tile], 1
                 if planes == 1:
                     A = A32.bfloat16().contiguous()
                     W = W32.bfloat16().contiguous()
@@ -101,13 +107,14 @@ def main():
                 resid = torch.zeros((M, N), device=dev) if epi == EPI["resid"] else None
 
                 def run(sync=0):
-                    return L.laya_b200_gemm(ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(W.data_ptr()),
-                                            ctypes.c_void_p(out.data_ptr()),
-                                            ctypes.c_void_p(resid.data_ptr()) if resid is not None else None, None,
-                                            M, N, K, planes, epi, out_mode, 0, bn, ctypes.c_void_p(cos.data_ptr()),
-                                            ctypes.c_void_p(sin.data_ptr()), ctypes.c_void_p(pos.data_ptr()),
-                                            2 * (N // 3) // 64 * 64 if epi == EPI["rope"] else 0, I,
-                                            ctypes.c_void_p(st), sync)
+                    args = (ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(W.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                            ctypes.c_void_p(resid.data_ptr()) if resid is not None else None, None,
+                            M, N, K, planes, epi, out_mode, 0, bn, ctypes.c_void_p(cos.data_ptr()),
+                            ctypes.c_void_p(sin.data_ptr()), ctypes.c_void_p(pos.data_ptr()),
+                            2 * (N // 3) // 64 * 64 if epi == EPI["rope"] else 0, I)
+                    if splits > 1:  # the K loop in slices, partials summed by the reduce kernel
+                        return L.laya_b200_gemm_splitk(*args, splits, ctypes.c_void_p(st), sync)
+                    return L.laya_b200_gemm(*args, ctypes.c_void_p(st), sync)
                 rc = run(1)
                 assert rc == 0, rc
                 err = None
@@ -127,7 +134,8 @@ def main():
                 torch.cuda.synchronize()
                 ms = e0.elapsed_time(e1) / a.iters
                 tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
-                row = {"M": M, "K": K, "N": N, "mode": mode, "epi": a.epi, "tile": bn, "ms": ms, "tflops": tf,
+                row = {"M": M, "K": K, "N": N, "mode": mode, "epi": a.epi, "tile": bn, "splits": splits, "ms": ms,
+                       "tflops": tf, "out": "f32" if out_mode == 2 else "bf16",
                        "frac_sustained": tf / sus, "frac_burst": tf / burst, "max_rel_err": err}
                 if mode == "bf16" and not a.no_cublas:
                     Ab, Wb = A32.bfloat16(), W32.bfloat16()
@@ -146,8 +154,8 @@ def main():
                 if a.json:
                     print(json.dumps(row), flush=True)
                 else:
-                    print("M=%6d K=%5d N=%5d %-6s tile=%d %8.3f ms %7.1f TF/s (%.2f sust, %.2f burst) cublas=%s err=%s"
-                          % (M, K, N, mode, bn, ms, tf, tf / sus, tf / burst,
+                    print("M=%6d K=%5d N=%5d %-6s tile=%d splits=%d %8.3f ms %7.1f TF/s (%.2f sust, %.2f burst) cublas=%s err=%s"
+                          % (M, K, N, mode, bn, splits, ms, tf, tf / sus, tf / burst,
                              "%.1f" % row["cublas_tflops"] if "cublas_tflops" in row else "-",
                              "%.2e" % err if err is not None else "-"), flush=True)
                 del A, W, out, resid

@@ -48,13 +48,22 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--calls", type=int, default=50, help="full-batch calls for the per-call latency")
     ap.add_argument("--batch1-calls", type=int, default=200, help="C1-shape calls for the batch-1 latency (c4)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="questions per call (default: the configuration's B); e.g. 8x B over 8 GPUs gives every "
+                         "GPU about one configuration's load through one handle")
     args = ap.parse_args(argv)
     arch_name, gen, desc = CONFIGS[args.workload]
     arch = synth.ARCHS[arch_name]
     ck = synth.checkpoint(arch_name, 0)
-    qs = gen(arch)
+    qs = gen(arch, B=args.batch) if args.batch > 0 else gen(arch)
+    if args.batch > 0:
+        desc += "; B=%d questions per call" % args.batch
     lens, ids, nmark, markers, qtypes = workloads.flatten(qs)
-    os.environ.setdefault("LAYA_MAX_TOKENS", str(max(131072, int(lens.sum()) + 4096)))
+    # one pass per replica: the replica's share of the rows (longest-first assignment keeps every
+    # replica within about one question of the mean) with room to spare
+    ndev_req = len([d for d in args.devices.split(",") if d.strip()])
+    per_dev = int(lens.sum()) // max(1, ndev_req) * 5 // 4 + 4096
+    os.environ.setdefault("LAYA_MAX_TOKENS", str(max(131072, per_dev)))
     L = load_lib()
     h = L.laya_create_ex(ck.encode(), 0, args.devices.encode())
     if not h:
