@@ -293,6 +293,7 @@ class Replica {
   CUtensorMap out_qkv, out_mg, out_ff, out_ffg, out_x, out_xg, out_hs;
   CUtensorMap qkv_map, qkv_map64;  // bf16 qkv rows as TMA sources of the tcgen05 attention (Q / K,V boxes)
   bool attn_tc = false;
+  bool attn_small = true;  // LAYA_ATTN_SMALL=0: the tcgen05 attention for small passes too
   int* d_attn_ticket = nullptr;  // work counter of the persistent attention kernel
   float* xg = nullptr;
   void* hs = nullptr;
@@ -513,6 +514,7 @@ class Replica {
     // they must hold finite values; dalloc zeroes every buffer, and later passes only ever leave
     // finite GEMM results there.
     attn_tc = P == 1 && !(getenv("LAYA_ATTN_MMA_SYNC") && atoi(getenv("LAYA_ATTN_MMA_SYNC")) != 0);
+    attn_small = env_int("LAYA_ATTN_SMALL", 1) != 0;
     if (attn_tc && (!make_operand_map(&qkv_map, qkv, 3 * (uint64_t)D, Tcap, 1, 128) ||
                     !make_operand_map(&qkv_map64, qkv, 3 * (uint64_t)D, Tcap, 1, 64))) {
       *err = "qkv tensor map rejected";
@@ -749,10 +751,18 @@ class Replica {
   }
 
   // Attention of every packed row into `ao`: the tcgen05 kernel over 128-row items in bf16 mode,
-  // the mma.sync / fp32 kernels over 64-row items otherwise (parity mode, or LAYA_ATTN_MMA_SYNC=1).
+  // the mma.sync / fp32 kernels over 64-row items otherwise (parity mode, LAYA_ATTN_MMA_SYNC=1, or a
+  // small pass). Small passes: the tcgen05 kernel's 128-row units x heads leave most SMs idle and each
+  // unit is a serial chain over its keys, so the mma.sync kernel's 64-row items (one CTA each) finish
+  // sooner. Measured on a B200 with 512-token sequences (sliding / global layers, µs per launch): 512
+  // rows 9.3 / 12.8 tcgen05 against 5.8 / 10.6 mma.sync, 1024 rows 9.4 / 13.2 against 7.5 / 14.8,
+  // 2048 rows 11.0 / 15.2 against 12.2 / 30.0; hence the mma.sync kernel for sliding layers up to
+  // kAttnSmallSliding rows and for global layers up to kAttnSmallGlobal rows.
+  static constexpr int kAttnSmallSliding = 1024, kAttnSmallGlobal = 512;
   void attend_rows(const AttnItem* items, int n_items, const AttnItem* items128, int n_items128, const int* soff,
                    const int* slen, int window) {
-    if (!attn_tc) {
+    const bool small = pass_rows <= (window > 0 ? kAttnSmallSliding : kAttnSmallGlobal) && attn_small;
+    if (!attn_tc || small) {
       attend(items, n_items, soff, slen, window, ao.p, ao.plane, nullptr, nullptr);
       return;
     }

@@ -223,10 +223,14 @@ def test_large_255_markers(large_bf16, large_oracle):
 
 
 def test_multipass_equals_single_pass(tiny_ckpt):
+    """Packing invariance: the same questions cut into many small passes give the single pass's
+    results. The attention kernel is pinned (LAYA_ATTN_SMALL=0), since small passes would otherwise
+    take the mma.sync attention, whose bf16 rounding differs (checked separately)."""
     a = synth.ARCHS["tiny"]
     qs = workloads.mixed(a, 60, seed=11, kmax=8)
-    one = Handle(tiny_ckpt, 0, env={"LAYA_MAX_TOKENS": 16384})
-    many = Handle(tiny_ckpt, 0, env={"LAYA_MAX_TOKENS": 16384, "LAYA_PASS_TOKENS": 300, "LAYA_MAX_SEQS": 5})
+    one = Handle(tiny_ckpt, 0, env={"LAYA_MAX_TOKENS": 16384, "LAYA_ATTN_SMALL": 0})
+    many = Handle(tiny_ckpt, 0, env={"LAYA_MAX_TOKENS": 16384, "LAYA_PASS_TOKENS": 300, "LAYA_MAX_SEQS": 5,
+                                     "LAYA_ATTN_SMALL": 0})
     try:
         rc1, lo1, ac1 = one.forward(qs)
         rc2, lo2, ac2 = many.forward(qs)
@@ -235,6 +239,26 @@ def test_multipass_equals_single_pass(tiny_ckpt):
     finally:
         one.close()
         many.close()
+
+
+def test_small_pass_attention_choice_matches_tcgen05_path(large_ckpt, large_oracle):
+    """Passes of at most 1024 rows run the sliding-window layers (and at 512 rows the global ones) on
+    the mma.sync attention kernel. At batch 1 (C1 shape, 512 rows) its results agree with the tcgen05
+    path and with the oracle at the bf16 tolerance (probability delta < 0.01, act < 0.05)."""
+    qs = workloads.c1(synth.ARCHS["large"])
+    small = Handle(large_ckpt, 0, env={"LAYA_MAX_TOKENS": 4096})
+    tc = Handle(large_ckpt, 0, env={"LAYA_MAX_TOKENS": 4096, "LAYA_ATTN_SMALL": 0})
+    try:
+        r1, r2 = small.forward(qs), tc.forward(qs)
+    finally:
+        small.close()
+        tc.close()
+    assert r1[0] == 0 and r2[0] == 0
+    assert not np.array_equal(r1[1], r2[1])  # the two kernels really ran
+    lo_o, ac_o, _ = large_oracle.forward_batch(qs)
+    for lo, ac in ((r1[1], r1[2]), (r2[1], r2[2])):
+        assert prob_delta(lo, lo_o, qs) < 0.01 and act_rel(ac, ac_o) < 0.05
+    assert prob_delta(r1[1], r2[1], qs) < 0.01
 
 
 def test_graph_replay_is_bitwise_stable(tiny_ckpt):
