@@ -13,6 +13,7 @@ bf16 rows write fp32 for that check; ``--no-check`` writes bf16 as cuBLAS does (
 
 Usage: python -m layamd_b200.gemm_sweep [--m 512,4096] [--kn 1024x3072,...] [--epi store|geglu|rope|resid]
        [--modes bf16,parity] [--tile auto|128|256|pair] [--iters 20] [--no-check] [--json]
+       python -m layamd_b200.gemm_sweep --sustained 3    # the C2 pass's GEMMs at the power cap vs cuBLAS
 """
 import argparse
 import ctypes
@@ -52,6 +53,59 @@ def interleave_geglu(W, I):
     return torch.cat(parts).contiguous()
 
 
+def sustained(L, seconds, rows=52287):
+    """The C2 pass's four encoder GEMMs (QKV, attention-out, MLP-in, MLP-out at `rows` rows) run back
+    to back for `seconds` each way, so that the GPU settles at its power cap as inside a long pass:
+    cuBLAS (torch.matmul, bf16 output), this library with a plain bf16 store, and this library with the
+    pass's fused epilogues (RoPE on QKV, fp32 residual add on the two residual GEMMs, GeGLU on MLP-in).
+    Prints one line per run: ms per set of four and TFLOP/s (2MNK summed over the four)."""
+    import time
+    import torch
+    shapes = [(1024, 3072), (1024, 1024), (1024, 5248), (2624, 1024)]  # (K, N)
+    M = rows
+    g = torch.Generator(device="cuda").manual_seed(5)
+    A = {K: torch.randn(M, K, device="cuda", generator=g).bfloat16() for K in (1024, 2624)}
+    W = [(0.02 * torch.randn(N, K, device="cuda", generator=g)).bfloat16() for K, N in shapes]
+    O = [torch.empty(M, N, device="cuda", dtype=torch.bfloat16) for K, N in shapes]
+    x = torch.zeros(M, 1024, device="cuda")
+    pos = torch.randint(0, 512, (M,), device="cuda", dtype=torch.int32, generator=g)
+    cs = torch.rand(512, 32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    flops = sum(2.0 * M * N * K for K, N in shapes)
+    vp = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+
+    def ours(fused):
+        for i, (K, N) in enumerate(shapes):
+            epi, out, res = ((1, O[i], None), (3, None, x), (2, O[i], None), (3, None, x))[i] if fused else (0, O[i], None)
+            bn, _ = plan(L, M, N, K, sms, False)
+            rc = L.laya_b200_gemm(vp(A[K]), vp(W[i]), vp(out), vp(res), None, M, N, K, 1, epi, 0, 0, bn, vp(cs), vp(cs),
+                                  vp(pos), 2 * (N // 3) // 64 * 64 if epi == 1 else 0, N // 2, ctypes.c_void_p(st), 0)
+            assert rc == 0, rc
+
+    def cublas():
+        for i, (K, N) in enumerate(shapes):
+            torch.matmul(A[K], W[i].T, out=O[i])
+
+    for name, f in (("cublas", cublas), ("laya-store", lambda: ours(False)), ("laya-fused", lambda: ours(True))) * 2:
+        for _ in range(3):
+            f()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n, t0 = 0, time.time()
+        e0.record()
+        while time.time() - t0 < seconds:
+            for _ in range(10):
+                f()
+            n += 10
+            torch.cuda.synchronize()
+        e1.record()
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / n
+        print("%-10s M=%d: %.3f ms per set of four, %.1f TFLOP/s sustained" % (name, M, ms, flops / (ms / 1e3) / 1e12),
+              flush=True)
+
+
 def main():
     import torch
     from layamd_b200 import load_lib
@@ -66,8 +120,13 @@ def main():
     ap.add_argument("--no-check", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--json", action="store_true")
+    ap.add_argument("--sustained", type=float, default=0.0,
+                    help="seconds: instead of the sweep, the C2 pass's four GEMMs back to back at the power cap, "
+                         "cuBLAS vs this library (plain store and fused epilogues)")
     a = ap.parse_args()
     L = load_lib()
+    if a.sustained > 0:
+        return sustained(L, a.sustained)
     dev = torch.device("cuda:0")
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     sus, burst = peaks()
