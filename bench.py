@@ -11,11 +11,13 @@ Per step (one forward pass over the 192 questions):
          CUDA graph, timed with CUDA events on the engine's stream (laya_replay), max over ranks;
   e2e    decisions/s through the public C ABI (laya_forward_batch) from host arrays: packing,
          host->device upload, the pass and the device->host read of the logits every step.
-  roofline  the encoder GEMM family: algorithmic 2*M*N*K FLOPs of one pass over their device time,
-         from CUDA events around every stage inside the replayed pass graph (laya_replay_profiled),
-         against the measured sustained bf16 peak of MEASURED_PEAKS.json.
-  hbm_roofline  the bandwidth-bound stages (attention, LayerNorm, embedding) the same way: algorithmic
-         bytes over in-graph device time against the measured HBM copy bandwidth.
+  roofline  the tensor-bound encoder GEMMs (QKV, MLP-in, MLP-out): algorithmic 2*M*N*K FLOPs of one
+         pass over their device time, from CUDA events around every stage inside the replayed pass
+         graph (laya_replay_profiled), against the measured sustained bf16 peak of
+         MEASURED_PEAKS.json; all_encoder_gemms adds the attention out-projection.
+  hbm_roofline  the bandwidth-bound stages (attention, LayerNorm, embedding, the attention
+         out-projection with its fp32 residual) the same way: algorithmic bytes over in-graph device
+         time against the measured HBM copy bandwidth.
   seq512 the fixed-length shape of the metric's name: 128 questions x 512 tokens x 3 options per
          rank, resident in HBM and replayed like value (a named extra; value stays C2).
 Multi-GPU (torchrun, one rank per GPU): every rank serves its own copy of the 192 questions on its own GPU;
@@ -196,6 +198,8 @@ def hbm_rooflines(qs, arch, prof):
       LayerNorm (ln stage)     read x fp32 (4D) + write xn bf16 (2D) = 6D per row; the last one of
                                the encoder also writes x back (final norm + type embedding), +4D
       embedding + LayerNorm    read the fp32 embedding row (4D) + write x (4D) + xn (2D) = 10D
+      attention out-projection read the bf16 attention rows (2D) + read and write the fp32 residual
+      (gemm_attn_out)          (8D) = 10D per row, plus its D x D bf16 weight once per launch
     """
     T = sum(len(q["ids"]) for q in qs)
     D = arch.d
@@ -206,6 +210,7 @@ def hbm_rooflines(qs, arch, prof):
         "attn_sliding": lambda n: n * 8 * D * T,
         "ln": lambda n: n * 6 * D * T + (4 * D * T if n else 0),
         "embed_ln": lambda n: n * 10 * D * T,
+        "gemm_attn_out": lambda n: n * (10 * D * T + 2 * D * D),
     }
     for name, fn in spec.items():
         if name not in prof or prof[name][0] <= 0:
@@ -377,16 +382,25 @@ def main():
     # ---- roofline of the dominant kernel (the tcgen05 GEMM): per-stage CUDA events inside the
     # replayed pass graph, right after the timed region and the end-to-end calls (steady clocks)
     prof = profiled_stage_times(L, h)
+    # The tensor-bound family is QKV (+RoPE), MLP-in (+GeGLU) and MLP-out (+residual, K = I): the
+    # attention out-projection (K = D, fp32 residual read-modify-write) needs as long for its bytes
+    # at the measured HBM bandwidth as for its FLOPs at the tensor peak, so it is reported with the
+    # HBM-bound stages (hbm_rooflines) and, for completeness, in the four-GEMM figure below.
     fl = encoder_gemm_flops(qs, arch)
-    g_ms = sum(prof[k][0] for k in fl if k in prof)
-    g_launch = sum(prof[k][1] for k in fl if k in prof)
-    achieved = sum(fl.values()) / (g_ms / 1e3) / 1e12 if g_ms > 0 else None
+    tensor_gemms = ("gemm_qkv", "gemm_mlp_in", "gemm_mlp_out")
+    g_ms = sum(prof[k][0] for k in tensor_gemms if k in prof)
+    g_launch = sum(prof[k][1] for k in tensor_gemms if k in prof)
+    achieved = sum(fl[k] for k in tensor_gemms) / (g_ms / 1e3) / 1e12 if g_ms > 0 else None
+    all_ms = sum(prof[k][0] for k in fl if k in prof)
+    all4 = sum(fl.values()) / (all_ms / 1e3) / 1e12 if all_ms > 0 else None
     peak, peak_src = load_peaks()
     traffic = None
     tr_path = os.path.join(ROOT, "profiles", "gemm_traffic.json")
     if os.path.exists(tr_path):
-        try:
-            traffic = json.load(open(tr_path)).get("bytes_per_launch")
+        try:  # mean DRAM bytes per launch of the three tensor-bound classes (one ncu capture)
+            per = json.load(open(tr_path))["per_launch_bytes"]
+            vals = [v for k, v in per.items() if k.split()[0] in tensor_gemms]
+            traffic = sum(vals) / len(vals) if len(vals) == len(tensor_gemms) else None
         except Exception:
             traffic = None
 
@@ -450,8 +464,11 @@ def main():
             "gpu_launches": int(launches.value),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": (achieved / peak) if achieved else None, "traffic": traffic,
-                         "kernel": "gemm_tc_kernel (encoder QKV/out/MLP-in/MLP-out), %d launches per step, %.3f ms"
-                                   % (g_launch, g_ms), "peak_source": peak_src},
+                         "kernel": "gemm_tc_kernel (encoder QKV+RoPE / MLP-in+GeGLU / MLP-out+residual), %d launches "
+                                   "per step, %.3f ms" % (g_launch, g_ms), "peak_source": peak_src,
+                         "all_encoder_gemms": {"achieved": all4, "frac": (all4 / peak) if all4 else None,
+                                               "ms": round(all_ms, 4),
+                                               "note": "the four classes with the attention out-projection"}},
             "model_flops_per_step": decision_flops(qs, arch),
             "model_tflops": decision_flops(qs, arch) * world / (dev_ms / args.steps / 1e3) / 1e12,
             "hbm_roofline": hbm_rooflines(qs, arch, prof),

@@ -55,8 +55,9 @@ def split(x):
 
 @pytest.mark.parametrize("bn", [128, 256, 512])
 @pytest.mark.parametrize("M,N,K", [(1, 256, 64), (127, 512, 1024), (300, 1024, 72), (1024, 3072, 1024),
-                                   (520, 1024, 2624), (4096, 768, 1152)])
+                                   (520, 1024, 2624), (4096, 768, 1152), (600, 1152, 1024), (2000, 640, 320)])
 def test_store_f32(L, bn, M, N, K):
+    """N = 1152 and 640 end in a half-filled 256-column tile."""
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
     A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
     W = (0.02 * torch.randn(N, K, device="cuda", generator=g)).bfloat16()
