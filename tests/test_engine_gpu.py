@@ -7,6 +7,7 @@ Tolerances, as the parity contract states them:
   bf16 mode         argmax of every question equal to the oracle's; probability delta < 0.01 and act
                     relative error < 0.05 (the reference's own row tolerance, src/test_parity.cpp:69)
 """
+import ctypes
 import os
 
 import numpy as np
@@ -188,11 +189,25 @@ def test_validation_contract(tiny_bf16):
         [dict(good[1], markers=[len(good[1]["ids"])])],                       # marker == len
         [dict(good[1], markers=[-1])],                                        # marker < 0
         [dict(good[2], ids=[5] * 120, markers=[1] * 256)],                    # 256 markers
+        [dict(good[0], ids=[a.vocab] + good[0]["ids"][1:])],                  # id past the vocabulary
+        [dict(good[0], ids=[-1] + good[0]["ids"][1:])],                       # negative id
+        [good[0], dict(good[1], qtype=3)],                                    # unknown question type
     ]
     for qs in bad_cases:
         rc, lo, ac = tiny_bf16.forward(qs)
         assert rc == -1
         assert np.isnan(ac).all()  # outputs untouched
+    # an empty batch is a successful no-op (the reference's loops simply do not run,
+    # src/engine.hip:491-497), and the next call is unaffected
+    one = np.zeros(1, np.int32)
+    lo0 = np.full(1, np.nan, np.float32)
+    ac0 = np.full((1, tiny_bf16.n_act), np.nan, np.float32)
+    IPt, FPt = ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_float)
+    assert tiny_bf16.L.laya_forward_batch(tiny_bf16.h, 0, *[one.ctypes.data_as(IPt)] * 5,
+                                          lo0.ctypes.data_as(FPt), ac0.ctypes.data_as(FPt)) == 0
+    assert np.isnan(lo0).all() and np.isnan(ac0).all()
+    rc, lo, ac = tiny_bf16.forward(good)
+    assert rc == 0 and np.isfinite(lo).all() and np.isfinite(ac).all()
 
 
 def test_255_markers_and_one_token(tiny_fp32, tiny_oracle):
