@@ -179,6 +179,18 @@ def test_large_c2_bf16_all_192_vs_reference(large_bf16):
     assert argmax_agree(lo, g["logits"], qs)
 
 
+def test_large_c2_fp32_parity_all_192_vs_reference(large_fp32):
+    """The same 192 questions in fp32-parity mode, at the parity contract's tolerance, through an
+    engine whose 16,384-row passes split the 52,287-token batch into several passes."""
+    qs = workloads.c2(synth.ARCHS["large"])
+    g = np.load(os.path.join(GOLD, "large_c2_logits.npz"))
+    rc, lo, ac = large_fp32.forward(qs)
+    assert rc == 0
+    assert prob_delta(lo, g["logits"], qs) <= 1e-4
+    assert act_rel(ac, g["act"]) <= 1e-3
+    assert argmax_agree(lo, g["logits"], qs)
+
+
 def test_validation_contract(tiny_bf16):
     a = synth.ARCHS["tiny"]
     good = workloads.mixed(a, 3, seed=7, kmax=3)
