@@ -7,6 +7,7 @@ ModernBertModel; neither exists on the GPU boxes, which only read the committed 
     python tests/golden/make_golden.py              # every fixture
     python tests/golden/make_golden.py --configs    # only the C3 / C4 ones
     python tests/golden/make_golden.py --c2         # only the C2 batch's logits
+    python tests/golden/make_golden.py --c3c4       # only the whole C3 and C4 batches' logits
 
 What it does, following ref/gen_golden.py:51-105 of the reference:
   1. builds each synthetic checkpoint with layamd_b200.synthetic.synth (seeded init rule) and checks that the
@@ -154,6 +155,7 @@ def main():
     del model
     configs()
     c2_batch()
+    c3c4_batches()
 
 
 def configs():
@@ -190,11 +192,21 @@ def c2_batch():
     """Logits and act logits of the reference for the whole C2 benchmark batch (ModernBERT-large, 64
     states x 3 questions, seed 1), run in length-sorted padded batches of 16 as predict_items does
     (ref/rl_common.py:370-408); no hooks."""
-    import torch
-    a = synth.ARCHS["large"]
-    ck = synth.checkpoint("large", 0)
+    batch_logits("large", workloads.c2(synth.ARCHS["large"], seed=1), "large_c2_logits.npz")
+
+
+def c3c4_batches():
+    """The same for the whole C3 batch (mmBERT-base, 128 questions, L ~ U[64,1024], seed 3) and the
+    whole C4 batch (ModernBERT-large at context 1024, 256 questions, L log-uniform in [128,1024],
+    seed 4), the batches workload_bench serves."""
+    batch_logits("base", workloads.c3(synth.ARCHS["base"], seed=3), "base_c3_logits.npz")
+    batch_logits("large1024", workloads.c4(synth.ARCHS["large1024"], seed=4), "large1024_c4_logits.npz")
+
+
+def batch_logits(arch_name, qs, out_name):
+    a = synth.ARCHS[arch_name]
+    ck = synth.checkpoint(arch_name, 0)
     model, rl, w = reference_model(ck)
-    qs = workloads.c2(a, seed=1)
     order = sorted(range(len(qs)), key=lambda i: len(qs[i]["ids"]))
     logits = [None] * len(qs)
     act = np.zeros((len(qs), a.n_act), np.float32)
@@ -205,17 +217,18 @@ def c2_batch():
             logits[i] = lo[r, :len(qs[i]["markers"])]
             act[i] = ac[r]
     lens, ids, nmark, markers, qtypes = workloads.flatten(qs)
-    np.savez_compressed(os.path.join(HERE, "large_c2_logits.npz"), lens=lens, nmark=nmark, qtypes=qtypes,
+    np.savez_compressed(os.path.join(HERE, out_name), lens=lens, nmark=nmark, qtypes=qtypes,
                         markers=markers, ids_sum=np.int64(ids.astype(np.int64).sum()),
                         logits=np.concatenate(logits).astype(np.float32), act=act)
-    print("[golden] large_c2_logits: %d questions, %d tokens" % (len(qs), int(lens.sum())), flush=True)
+    print("[golden] %s: %d questions, %d tokens" % (out_name, len(qs), int(lens.sum())), flush=True)
 
 
 if __name__ == "__main__":
-    if sys.argv[1:] in (["--configs"], ["--c2"]):
+    steps = {"--configs": configs, "--c2": c2_batch, "--c3c4": c3c4_batches}
+    if len(sys.argv) == 2 and sys.argv[1] in steps:
         import torch
         torch.set_grad_enabled(False)
         torch.set_num_threads(os.cpu_count() or 8)
-        configs() if sys.argv[1] == "--configs" else c2_batch()
+        steps[sys.argv[1]]()
     else:
         main()

@@ -112,3 +112,29 @@ def test_fp32_parity_against_reference_golden(arch, case):
     worst["head1"] = rel(np.linalg.norm(t, axis=-1), g["n_head1"][idx])
     bad = {k: v for k, v in worst.items() if v > 1e-3}
     assert not bad, bad
+
+
+@pytest.mark.parametrize("arch,workload,case", [("base", "c3", "base_c3_logits"),
+                                                ("large1024", "c4", "large1024_c4_logits")])
+def test_whole_benchmark_batch_against_reference(arch, workload, case):
+    """The whole batch workload_bench serves at C3 (128 mmBERT-base questions, L ~ U[64,1024]) and C4
+    (256 ModernBERT-large context-1024 questions, L log-uniform in [128,1024]) through one
+    laya_forward_batch call, against the reference's logits for the same questions
+    (tests/golden/<case>.npz, made by make_golden.py --c3c4): fp32-parity mode at the parity contract's
+    tolerance and bf16 at the reference's row tolerance with the argmax rule."""
+    ck = synth.checkpoint(arch, 0)
+    qs = getattr(workloads, workload)(synth.ARCHS[arch])
+    g = np.load(os.path.join(GOLD, case + ".npz"))
+    lens, ids, nmark, markers, qtypes = workloads.flatten(qs)
+    assert (lens == g["lens"]).all() and (nmark == g["nmark"]).all() and (markers == g["markers"]).all()
+    assert int(ids.astype(np.int64).sum()) == int(g["ids_sum"])
+    for precision, dp, da in ((1, 1e-4, 1e-3), (0, 0.01, 0.05)):
+        h = Handle(ck, precision, env={"LAYA_MAX_TOKENS": 65536})
+        try:
+            rc, lo, ac = h.forward(qs)
+        finally:
+            h.close()
+        assert rc == 0
+        assert prob_delta(lo, g["logits"], qs) <= dp, precision
+        assert act_rel(ac, g["act"]) <= da, precision
+        assert argmax_agree(lo, g["logits"], qs), precision
