@@ -8,6 +8,7 @@ ModernBertModel; neither exists on the GPU boxes, which only read the committed 
     python tests/golden/make_golden.py --configs    # only the C3 / C4 ones
     python tests/golden/make_golden.py --c2         # only the C2 batch's logits
     python tests/golden/make_golden.py --c3c4       # only the whole C3 and C4 batches' logits
+    python tests/golden/make_golden.py --seq512     # only the fixed-length 512 batch's logits
 
 What it does, following ref/gen_golden.py:51-105 of the reference:
   1. builds each synthetic checkpoint with layamd_b200.synthetic.synth (seeded init rule) and checks that the
@@ -156,6 +157,7 @@ def main():
     configs()
     c2_batch()
     c3c4_batches()
+    seq512_batch()
 
 
 def configs():
@@ -203,6 +205,12 @@ def c3c4_batches():
     batch_logits("large1024", workloads.c4(synth.ARCHS["large1024"], seed=4), "large1024_c4_logits.npz")
 
 
+def seq512_batch():
+    """The same for the bench's fixed-length batch (128 choice questions of exactly 512 tokens with 3
+    options, seed 5)."""
+    batch_logits("large", workloads.seq512(synth.ARCHS["large"], seed=5), "large_seq512_logits.npz")
+
+
 def batch_logits(arch_name, qs, out_name):
     a = synth.ARCHS[arch_name]
     ck = synth.checkpoint(arch_name, 0)
@@ -224,7 +232,7 @@ def batch_logits(arch_name, qs, out_name):
 
 
 if __name__ == "__main__":
-    steps = {"--configs": configs, "--c2": c2_batch, "--c3c4": c3c4_batches}
+    steps = {"--configs": configs, "--c2": c2_batch, "--c3c4": c3c4_batches, "--seq512": seq512_batch}
     if len(sys.argv) == 2 and sys.argv[1] in steps:
         import torch
         torch.set_grad_enabled(False)

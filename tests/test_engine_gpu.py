@@ -179,6 +179,22 @@ def test_large_c2_bf16_all_192_vs_reference(large_bf16):
     assert argmax_agree(lo, g["logits"], qs)
 
 
+def test_seq512_batch_bf16_vs_reference(large_bf16):
+    """The bench's fixed-length batch (128 choice questions of exactly 512 tokens, 3 options each)
+    in one bf16 call, against the reference's logits for it (tests/golden/large_seq512_logits.npz,
+    made by make_golden.py --seq512)."""
+    qs = workloads.seq512(synth.ARCHS["large"])
+    g = np.load(os.path.join(GOLD, "large_seq512_logits.npz"))
+    lens, ids, nmark, markers, qtypes = workloads.flatten(qs)
+    assert (lens == g["lens"]).all() and (markers == g["markers"]).all()
+    assert int(ids.astype(np.int64).sum()) == int(g["ids_sum"])
+    rc, lo, ac = large_bf16.forward(qs)
+    assert rc == 0
+    assert prob_delta(lo, g["logits"], qs) < 0.01
+    assert act_rel(ac, g["act"]) < 0.05
+    assert argmax_agree(lo, g["logits"], qs)
+
+
 def test_large_c2_fp32_parity_all_192_vs_reference(large_fp32):
     """The same 192 questions in fp32-parity mode, at the parity contract's tolerance, through an
     engine whose 16,384-row passes split the 52,287-token batch into several passes."""

@@ -119,6 +119,21 @@ def test_c2_golden_inputs_are_the_benchmark_batch():
     assert np.isfinite(g["logits"]).all()
 
 
+@pytest.mark.parametrize("arch,workload,case,B", [("base", "c3", "base_c3_logits", 128),
+                                                  ("large1024", "c4", "large1024_c4_logits", 256),
+                                                  ("large", "seq512", "large_seq512_logits", 128)])
+def test_whole_batch_golden_inputs_are_the_benchmark_batches(arch, workload, case, B):
+    """The same for the reference logits of the whole C3, C4 and fixed-length-512 batches."""
+    from layamd_b200.synthetic import workloads
+    g = np.load(os.path.join(GOLD, case + ".npz"))
+    lens, ids, nmark, markers, qtypes = workloads.flatten(getattr(workloads, workload)(synth.ARCHS[arch]))
+    assert len(lens) == B
+    assert (lens == g["lens"]).all() and (nmark == g["nmark"]).all() and (qtypes == g["qtypes"]).all()
+    assert (markers == g["markers"]).all() and int(ids.astype(np.int64).sum()) == int(g["ids_sum"])
+    assert g["logits"].shape == (int(nmark.sum()),) and g["act"].shape == (B, 2)
+    assert np.isfinite(g["logits"]).all() and np.isfinite(g["act"]).all()
+
+
 @pytest.mark.slow
 def test_oracle_on_c2_questions_matches_reference_batch():
     """Three C2 questions (shortest, median, longest) through the oracle against the reference's
