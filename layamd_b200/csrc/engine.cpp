@@ -298,6 +298,8 @@ class Replica {
   float* xg = nullptr;
   void* hs = nullptr;
   float *d_logits = nullptr, *d_act = nullptr;
+  float* d_head_hid = nullptr;  // sliced act head of small batches: hidden units [Bcap, 256]
+  int* d_head_cnt = nullptr;    // and per-question arrival counters [Bcap]
   int* d_err = nullptr;
 
   // per-pass staging
@@ -536,6 +538,8 @@ class Replica {
     }
     if (!dalloc(&d_logits, (size_t)Rcap * 4, err)) return false;
     if (!dalloc(&d_act, (size_t)Bcap * cfg.n_act * 4, err)) return false;
+    if (!dalloc(&d_head_hid, (size_t)Bcap * 256 * 4, err)) return false;
+    if (!dalloc(&d_head_cnt, (size_t)Bcap * 4, err)) return false;
     if (!dalloc(&d_err, 16, err)) return false;
     if (!dalloc(&d_attn_ticket, 16, err)) return false;
     // Split-K (LAYA_SPLITK=0 turns it off): when the 128 x 128 tiles of a GEMM cannot fill the
@@ -979,6 +983,8 @@ class Replica {
       a.b2 = a2B;
       a.logits = d_logits;
       a.act = d_act;
+      a.hid = d_head_hid;
+      a.hid_count = d_head_cnt;
       a.n_logits = KT;
       a.err = d_err;
       launched(head_out_launch(a, st));

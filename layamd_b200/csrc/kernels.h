@@ -242,6 +242,11 @@ struct HeadOutArgs {
   const float* b2 = nullptr;
   float* logits = nullptr;        // [sum nmark]
   float* act = nullptr;           // [B, n_act]
+  // Scratch of the sliced form (small batches: the act head's 256 hidden units of a question split
+  // over several CTAs): hidden values [B, 256] and per-question arrival counters [B], zero at
+  // allocation and left at zero by every launch. Null: one CTA per question.
+  float* hid = nullptr;
+  int* hid_count = nullptr;
   // extents the debug bounds mode checks the maps against (0: unchecked), and its error word
   int n_logits = 0;               // marker rows of hs / logit slots
   int* err = nullptr;

@@ -104,13 +104,20 @@ __device__ __forceinline__ float row_dot(const void* row, bool f32, const float*
   return warp_sum(s);
 }
 
+// Grid (B, S): CTA (b, s) computes question b's marker logits and softmax features, then hidden units
+// [s*256/S, (s+1)*256/S) of the act head. With S = 1 the CTA finishes the question alone; with S > 1
+// each slice stores its hidden units to a.hid, and the slice that arrives last on a.hid_count[b]
+// reads all 256 back, computes the outputs (in the same order as S = 1, so the results do not
+// depend on S) and resets the counter.
 __global__ void __launch_bounds__(256) head_out_kernel(const HeadOutArgs a) {
   __shared__ float s_logit[256];
   __shared__ __align__(16) float s_in[1024 + 8];
   __shared__ float s_hid[256];
+  __shared__ int s_last;
   pdl_trigger();
   pdl_wait();
   const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int S = gridDim.y, slice = blockIdx.y, rows = 256 / S;
   const int D = a.D, nm = a.nmark[b], mo = a.moff[b];
   if (!LAYA_IN_BOUNDS(nm >= 1 && nm <= 256 && mo >= 0 && (a.n_logits <= 0 || mo + nm <= a.n_logits), a.err,
                       kErrBoundsHead))
@@ -123,7 +130,7 @@ __global__ void __launch_bounds__(256) head_out_kernel(const HeadOutArgs a) {
     const float s = row_dot(hr, a.hs_f32 != 0, a.w3, D, lane) + a.b3;
     if (lane == 0) {
       s_logit[k] = s;
-      a.logits[mo + k] = s;
+      if (slice == 0) a.logits[mo + k] = s;
     }
   }
   for (int i = tid; i < D; i += 256) s_in[i] = a.cls[(long long)b * D + i];
@@ -151,7 +158,8 @@ __global__ void __launch_bounds__(256) head_out_kernel(const HeadOutArgs a) {
   // lane's (at most nine) 16-byte pieces of both rows in flight together
   const int K4 = (D + 4) / 4;  // D + 4 is a multiple of 4: every row starts 16-byte aligned
   const float4* s4 = reinterpret_cast<const float4*>(s_in);
-  for (int j = warp * 32; j < warp * 32 + 32; j += 2) {
+  const int per_warp = rows / 8;  // 32, 16, 8 or 4: even
+  for (int j = slice * rows + warp * per_warp; j < slice * rows + (warp + 1) * per_warp; j += 2) {
     const float4* r0 = reinterpret_cast<const float4*>(a.w0) + (long long)j * K4;
     const float4* r1 = r0 + K4;
     float4 w0[9], w1[9];
@@ -169,9 +177,25 @@ __global__ void __launch_bounds__(256) head_out_kernel(const HeadOutArgs a) {
     s0 = warp_sum(s0);
     s1 = warp_sum(s1);
     if (lane == 0) {
-      s_hid[j] = gelu_erf(s0 + a.b0[j]);
-      s_hid[j + 1] = gelu_erf(s1 + a.b0[j + 1]);
+      const float h0 = gelu_erf(s0 + a.b0[j]), h1 = gelu_erf(s1 + a.b0[j + 1]);
+      if (S == 1) {
+        s_hid[j] = h0;
+        s_hid[j + 1] = h1;
+      } else {
+        a.hid[(long long)b * 256 + j] = h0;
+        a.hid[(long long)b * 256 + j + 1] = h1;
+      }
     }
+  }
+  if (S > 1) {
+    __threadfence();  // this slice's hidden units are visible before its arrival is counted
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&a.hid_count[b], 1) == S - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    s_hid[tid] = __ldcg(a.hid + (long long)b * 256 + tid);  // 256 threads, 256 hidden units
+    if (tid == 0) a.hid_count[b] = 0;  // every slice has arrived: ready for the next launch
   }
   __syncthreads();
   for (int j = warp; j < a.n_act; j += 8) {
@@ -208,7 +232,18 @@ cudaError_t ln_launch(const LnArgs& a, cudaStream_t st) {
 cudaError_t head_out_launch(const HeadOutArgs& a, cudaStream_t st) {
   if (a.B <= 0) return cudaSuccess;
   if (a.D > 1024 || a.D % 128 != 0 || a.n_act > 256) return cudaErrorInvalidValue;  // 16-byte row pieces
-  return launch_pdl(head_out_kernel, dim3(a.B), dim3(256), 0, st, a);
+  // slices per question: as many of 8, 4, 2 as leave every slice an SM of its own
+  static const int sms = [] {  // the devices of one host are alike
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return 1;
+    return n;
+  }();
+  int S = 1;
+  if (a.hid && a.hid_count)
+    for (int s = 8; s > 1; s /= 2)
+      if (a.B * s <= sms) { S = s; break; }
+  return launch_pdl(head_out_kernel, dim3(a.B, S), dim3(256), 0, st, a);
 }
 
 }  // namespace laya
