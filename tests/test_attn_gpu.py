@@ -92,9 +92,10 @@ def test_tc_matches_mma_sync_full_width(L, window):
     assert rel(a[:T], b[:T]) < 1e-2
 
 
-def test_growing_scores_exercise_the_running_max(L):
+@pytest.mark.parametrize("window", [0, 64])
+def test_growing_scores_exercise_the_running_max(L, window):
     """Keys grow along the sequence so each 128-key chunk raises the row max by far more than 2^8:
-    the tensor-memory O accumulator must be rescaled chunk after chunk."""
+    the tensor-memory O accumulator must be rescaled chunk after chunk (inside the +-64 band too)."""
     lens = [1000, 700]
     H = 2
     qkv = make_qkv(lens, H, seed=11, scale=0.5).float()
@@ -107,10 +108,10 @@ def test_growing_scores_exercise_the_running_max(L):
         qkv[off:off + n, D:2 * D] = qkv[off:off + n, D:2 * D].abs()
         off += n
     qkv = qkv.bfloat16()
-    ref = reference(qkv, lens, H, 0)
+    ref = reference(qkv, lens, H, window)
     T = sum(lens)
     for impl in (0, 1):
-        out = run(L, qkv, lens, H, 0, impl)
+        out = run(L, qkv, lens, H, window, impl)
         assert rel(out[:T], ref[:T]) < 1e-2, impl
 
 
